@@ -1,0 +1,361 @@
+"""Benchmark of the fused MLP block (and the other fused workloads) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+One step = one pass of the hot path over one batch: for the default workload,
+the fused MLP block y = X + GELU(RMSNorm(X) @ W1 + b1) @ W2 at 8192 tokens x
+d=4096 x hidden=16384, bf16 I/O, fp32 accumulation, tanh GELU, eps 1e-5. Under
+torchrun each rank owns 8192 rows of a (8192 * N)-row batch with the weights
+replicated and no collective (weak scaling). Timing: W untimed warm-up steps,
+then exactly K steps between barrier + synchronize pairs, CUDA events on the
+launching stream, max over ranks. Inputs (W1 + W2 + X = 320 MiB) exceed the
+126 MB L2, so no flush is needed between steps.
+
+``--impl reference`` times the reference's CPU algorithm instead (the oracle's
+restatement of the reference golden, numpy/OpenBLAS on all host cores, exact-erf
+GELU through libm per element as the reference does), on a bounded row sample
+per step; under torchrun only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT), str(ROOT / "tt-flow_b200")]
+
+import numpy as np  # noqa: E402
+
+METRIC = "fused RMSNorm+MatMul / MLP TFLOP/s & % bf16 tensor peak at 1/2/4/8 B200"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# Bytes moved by the dominant kernel per launch, from the ncu capture summarised
+# in profiles/ (dram__bytes_read.sum + dram__bytes_write.sum); None until captured.
+TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+# ------------------------------------------------------------------ clock sampler
+
+
+class ClockSampler:
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str | None):
+        self.proc = None
+        self.path = None
+        if gpu_id is None or shutil.which("nvidia-smi") is None:
+            return
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        self.f = os.fdopen(fd, "w")
+        self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                      "-lms", "100", "-i", gpu_id], stdout=self.f, stderr=subprocess.DEVNULL)
+
+    def stop(self, t0: float, t1: float) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [s.strip() for s in line.split(",")]
+            if len(parts) < 10:
+                continue
+            try:
+                ts = time.mktime(time.strptime(parts[0].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                ts += float("0." + parts[0].split(".")[1]) if "." in parts[0] else 0.0
+                rows.append((ts, float(parts[2]), float(parts[3]), float(parts[4]), parts[6:10]))
+            except (ValueError, IndexError):
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        inside = [r for r in rows if t0 - 0.15 <= r[0] <= t1 + 0.15]
+        window = "timed"
+        if not inside:
+            inside = [r for r in rows if r[3] > 250.0] or rows
+            window = "warmup+timed (timed region shorter than the 100 ms sample period)"
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in inside for i, v in enumerate(r[4]) if v == "Active"})
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": max(r[2] for r in rows),
+                "power_w_max": max(r[3] for r in inside), "reasons": reasons, "samples": len(inside),
+                "window": window}
+
+
+def gpu_id_for_smi(dev: int) -> str | None:
+    import torch
+
+    try:
+        u = torch.cuda.get_device_properties(dev).uuid
+        s = str(u)
+        return s if s.startswith("GPU-") else f"GPU-{s}"
+    except Exception:
+        cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if cvd:
+            return cvd.split(",")[dev]
+        return str(dev)
+
+
+# -------------------------------------------------------------------- CPU leg
+
+
+def cpu_port_tflops(name: str, rows: int, reps: int = 1) -> tuple[float, float, dict]:
+    """Time the oracle's restatement of the reference golden on `rows` rows."""
+    from oracle import golden as O
+    from tfb200 import workloads as W
+
+    wl = W.WORKLOADS[name]
+    d = wl.dims
+    t = W.generate(name)
+    f = W.bf16_to_f32
+    rows = min(rows, d["M"])
+    times = []
+    if wl.kind == "fused_mlp":
+        x = f(t["x"][:rows])
+        args = (x, f(t["gamma"]), f(t["w1"]), f(t["b1"]), f(t["w2"]), x, wl.eps)
+        fl = 2 * rows * d["K"] * d["H"] + 2 * rows * d["H"] * d["N"]
+        for _ in range(reps):
+            s = time.perf_counter()
+            O.fused_mlp(*args, gelu_mode="erf")
+            times.append(time.perf_counter() - s)
+    elif wl.kind == "fused_rmsnorm_matmul":
+        x = f(t["x"][:rows])
+        fl = 2 * rows * d["K"] * d["N"]
+        for _ in range(reps):
+            s = time.perf_counter()
+            O.fused_rmsnorm_matmul(x, f(t["gamma"]), f(t["w"]), wl.eps)
+            times.append(time.perf_counter() - s)
+    else:
+        a = f(t["a"][:rows])
+        fl = 2 * rows * d["K"] * d["N"]
+        for _ in range(reps):
+            s = time.perf_counter()
+            O.matmul(a, f(t["b"]))
+            times.append(time.perf_counter() - s)
+    sec = statistics.median(times)
+    try:
+        from threadpoolctl import threadpool_info
+
+        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    except Exception:
+        cores = os.cpu_count() or 1
+    info = {"rows": rows, "seconds": sec, "cores": cores}
+    return fl / sec / 1e12, sec, info
+
+
+def run_reference(args) -> int:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from tfb200 import workloads as W
+
+    name = args.workload
+    rows = args.ref_rows
+    for _ in range(args.warmup):
+        cpu_port_tflops(name, rows)
+    vals, secs = [], []
+    info = {}
+    for _ in range(args.steps):
+        v, s, info = cpu_port_tflops(name, rows)
+        vals.append(v)
+        secs.append(s)
+    value = float(np.median(vals))
+    d = W.WORKLOADS[name].dims
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": float(np.median(secs)) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded numpy, bf16-rounded inputs)",
+        "config": {"workload": name, **d, "gelu": "erf (the reference golden's only form)", "eps": 1e-5,
+                   "sample_rows_per_step": info["rows"]},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": info["cores"], "kind": "port",
+                         "sample": f"{info['rows']} of {d['M']} rows per step, numpy/OpenBLAS fp32 matmuls, "
+                                   f"libm erf per element"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# -------------------------------------------------------------------- GPU leg
+
+
+def run_ours(args) -> int:
+    import torch
+    import torch.distributed as dist
+
+    from tfb200 import _lib, ops
+    from tfb200 import workloads as W
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    lib = _lib.lib()
+
+    name = args.workload
+    wl = W.WORKLOADS[name]
+    d = wl.dims
+    t = W.generate(name)
+
+    def dev(a):
+        return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda().view(torch.bfloat16)
+
+    if wl.kind == "fused_mlp":
+        x, g, w1, b1, w2 = (dev(t[k]) for k in ("x", "gamma", "w1", "b1", "w2"))
+        y = torch.empty(d["M"], d["N"], dtype=torch.bfloat16, device="cuda")
+        ws = torch.empty(ops.mlp_workspace_bytes(d["M"], d["K"], d["H"], d["N"]), dtype=torch.uint8, device="cuda")
+
+        def step(xin=None):
+            xx = x if xin is None else xin
+            ops.fused_mlp(xx, g, w1, b1, w2, xx, wl.eps, gelu=wl.gelu, out=y, workspace=ws)
+        in_bytes = x.numel() * 2
+    elif wl.kind == "fused_rmsnorm_matmul":
+        x, g, w = (dev(t[k]) for k in ("x", "gamma", "w"))
+        y = torch.empty(d["M"], d["N"], dtype=torch.bfloat16, device="cuda")
+
+        def step(xin=None):
+            ops.fused_rmsnorm_matmul(x if xin is None else xin, g, w, wl.eps, out=y)
+        in_bytes = x.numel() * 2
+    else:
+        x, b = dev(t["a"]), dev(t["b"])
+        y = torch.empty(d["M"], d["N"], dtype=torch.bfloat16, device="cuda")
+
+        def step(xin=None):
+            ops.matmul(x if xin is None else xin, b, out=y)
+        in_bytes = x.numel() * 2
+    flops_step = W.flops(name)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    sampler = ClockSampler(gpu_id_for_smi(local)) if rank == 0 else None
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    l0 = lib.tfb200_launch_count()
+    w0 = time.time()
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    w1t = time.time()
+    barrier()
+    launches = lib.tfb200_launch_count() - l0
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        tt = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    clocks = sampler.stop(w0, w1t) if sampler else None
+    ms_step = ms / args.steps
+    value = flops_step * world / (ms_step * 1e-3) / 1e12
+
+    # End to end through the public API with host buffers: pinned X in, Y out.
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+    xd = torch.empty_like(x)
+    for _ in range(max(1, args.warmup)):
+        xd.copy_(xh, non_blocking=True)
+        step(xd)
+        yh.copy_(y, non_blocking=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(args.steps):
+        xd.copy_(xh, non_blocking=True)
+        step(xd)
+        yh.copy_(y, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ems = e0.elapsed_time(e1)
+    if world > 1:
+        tt = torch.tensor([ems], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ems = float(tt.item())
+    e2e_value = flops_step * world / (ems / args.steps * 1e-3) / 1e12
+
+    pk, pk_src = peaks()
+    sustained = ms > 1000.0
+    peak = pk["bf16_tflops_sustained"] if sustained else pk["bf16_tflops"]
+    launches_per_step = max(1, launches // max(1, args.steps))
+    per_gpu = flops_step / (ms_step * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded numpy normal/uniform, bf16)",
+        "config": {"workload": name, **d, "gelu": wl.gelu, "eps": wl.eps, "rows_per_gpu": d["M"],
+                   "global_rows": d["M"] * world,
+                   "parallelism": f"rows sharded over {world} GPU(s), weights replicated, no collective",
+                   "l2": "inputs larger than L2 (no flush)"},
+        "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
+                     "frac": per_gpu / peak, "traffic": TRAFFIC_BYTES_PER_LAUNCH.get(name),
+                     "kernel": "k_gemm (persistent tcgen05 GEMM)", "launches_per_step": launches_per_step,
+                     "peak_source": f"{pk_src} {'sustained' if sustained else 'burst'} bf16 (MEASURED_PEAKS.json)"
+                     if pk_src == "measured" else "fallback"},
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": in_bytes,
+                "d2h_bytes_per_step": y.numel() * 2,
+                "note": "X copied in from pinned host memory and Y read back every step; weights resident"},
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        v, sec, info = cpu_port_tflops(name, args.cpu_rows)
+        line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": info["cores"], "kind": "port",
+                                "sample": f"{info['rows']} of {d['M']} rows in {sec:.1f} s: the reference golden "
+                                          f"restated (numpy/OpenBLAS fp32, libm erf per element)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="mlp_8192x4096x16384")
+    ap.add_argument("--cpu-rows", type=int, default=1024)
+    ap.add_argument("--ref-rows", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    return run_reference(args) if args.impl == "reference" else run_ours(args)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,123 @@
+/*
+ * tfb200.h -- C ABI of the B200 (sm_100a) backend for tt-flow's fused hot path:
+ * fused RMSNorm+MatMul, fused MLP block (RMSNorm, MatMul+bias+GELU, MatMul,
+ * residual add) and plain tiled MatMul.
+ *
+ * The reference (tensixflow) has no linked ABI for this path: its boundary is
+ * the op semantics of python/tensixflow/golden.py:97-122 (checked by the
+ * harness, python/tensixflow/harness.py:146-181) and the generated TT-Metalium
+ * host program, whose kernels the entry points below replace
+ * (lib/tensixflow/Codegen/EmitHost.cpp:100-575 matmul, :581-978 fused
+ * RMSNorm+MatMul, :980-1502 fused MLP). Each entry point cites the item it
+ * replaces.
+ *
+ * Conventions
+ *  - Matrices are row-major bf16 in device memory, described by tfb200_mat
+ *    (ld = leading dimension in elements, >= cols). Vectors (gamma, b1) are
+ *    contiguous bf16 device arrays.
+ *  - The caller owns every buffer; the library allocates no device memory and
+ *    never frees caller memory.
+ *  - Calls are asynchronous and ordered on `stream` (a cudaStream_t; NULL is the
+ *    legacy default stream). Distinct host threads may call concurrently on
+ *    distinct streams.
+ *  - Return value: TFB200_OK (0) or a negative TFB200_E* code; the message of the
+ *    last failure on the calling thread is in tfb200_last_error().
+ *  - Device-side waits are bounded. A kernel whose wait runs out returns early and
+ *    records TFB200_ETIMEOUT in a per-device status word read by
+ *    tfb200_device_status().
+ *  - No C++ exception crosses this boundary.
+ */
+#ifndef TFB200_H_
+#define TFB200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TFB200_ABI_VERSION 1
+
+enum tfb200_status {
+  TFB200_OK = 0,
+  TFB200_EINVAL = -1,       /* bad argument: null pointer, shape mismatch, bad ld */
+  TFB200_EUNSUPPORTED = -2, /* valid request this backend does not implement */
+  TFB200_ECUDA = -3,        /* a CUDA runtime / driver call failed */
+  TFB200_ETIMEOUT = -4,     /* a bounded device wait ran out */
+  TFB200_EWORKSPACE = -5,   /* workspace missing or smaller than required */
+  TFB200_ENOSPC = -6        /* output buffer (text) too small */
+};
+
+enum tfb200_dtype { TFB200_BF16 = 0, TFB200_F32 = 1 };
+
+enum tfb200_gelu { TFB200_GELU_ERF = 0, TFB200_GELU_TANH = 1 };
+
+/* A row-major matrix view: data[r * ld + c], r < rows, c < cols. */
+typedef struct tfb200_mat {
+  void* data;
+  int64_t rows;
+  int64_t cols;
+  int64_t ld;
+  int32_t dtype; /* enum tfb200_dtype; the kernels take TFB200_BF16 */
+} tfb200_mat;
+
+/* ABI version (TFB200_ABI_VERSION of the built library). */
+int tfb200_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* tfb200_last_error(void);
+
+/* C = A @ B, fp32 accumulation, bf16 output (round to nearest even).
+ * A [M,K], B [K,N], C [M,N]. Replaces the blocked-reuse / output-tile matmul
+ * kernels (EmitCompute.cpp:257-329, :560-650) and the matmul host program
+ * (EmitHost.cpp:100-575); semantics of golden.matmul (golden.py:56-60).
+ * K == 0 writes zeros; M == 0 or N == 0 is a no-op. */
+int tfb200_matmul(const tfb200_mat* a, const tfb200_mat* b, tfb200_mat* c, void* stream);
+
+/* Y = rmsnorm(X, gamma, eps) @ W with rmsnorm(x) = x / sqrt(mean_k(x^2) + eps) * gamma.
+ * X [M,K], gamma [K], W [K,N], Y [M,N]; K % 8 == 0. The inverse RMS is computed
+ * inside the GEMM from the staged activation tiles and applied to the fp32
+ * accumulator; the MMA consumes bf16(x * gamma).
+ * Replaces the fused RMSNorm+MatMul compute kernel (EmitCompute.cpp:60-255) and
+ * host program (EmitHost.cpp:581-978); semantics of golden.fused_rmsnorm_matmul
+ * (golden.py:97-102) and of the dialect op tensixflow.fused_rmsnorm_matmul
+ * (TensixflowOps.td:230-253; verifier TensixflowOps.cpp:197-278). */
+int tfb200_fused_rmsnorm_matmul(const tfb200_mat* x, const void* gamma, const tfb200_mat* w, float eps,
+                                tfb200_mat* y, void* stream);
+
+/* Bytes of device workspace tfb200_fused_mlp needs for M rows, K model width,
+ * H hidden width and N output width (the bf16 hidden activation block). */
+size_t tfb200_fused_mlp_workspace_size(int64_t m, int64_t k, int64_t h, int64_t n);
+
+/* Y = gelu(rmsnorm(X, gamma, eps) @ W1 + b1) @ W2 + R.
+ * X [M,K], gamma [K], W1 [K,H], b1 [H] (or NULL for no bias), W2 [H,N],
+ * R [M,N] (residual; may alias X when N == K), Y [M,N]. gelu_mode is
+ * TFB200_GELU_ERF (the reference's exact form) or TFB200_GELU_TANH.
+ * The hidden block is kept as bf16 in `workspace` (>= tfb200_fused_mlp_workspace_size
+ * bytes, 256-byte aligned).
+ * Replaces the fused MLP compute kernel (EmitCompute.cpp:331-558) and host
+ * program (EmitHost.cpp:980-1502); semantics of golden.fused_mlp
+ * (golden.py:105-122) and of tensixflow.fused_mlp (TensixflowOps.td:259-285;
+ * verifier TensixflowOps.cpp:284-413, which accepts a 1-D [H] bias). */
+int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w1, const void* b1,
+                     const tfb200_mat* w2, const tfb200_mat* residual, float eps, int gelu_mode, tfb200_mat* y,
+                     void* stream, void* workspace, size_t workspace_bytes);
+
+/* Device status word of the current device: TFB200_OK, or TFB200_ETIMEOUT if a
+ * kernel's bounded wait ran out since the last clear. Synchronises the device. */
+int tfb200_device_status(void);
+/* Reset the current device's status word to TFB200_OK. */
+int tfb200_clear_device_status(void);
+
+/* Wall-time limit of every bounded device wait, in nanoseconds (default 2e9). */
+void tfb200_set_wait_limit_ns(uint64_t ns);
+
+/* Number of kernels this library has launched in this process. */
+uint64_t tfb200_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TFB200_H_ */

@@ -1,0 +1,64 @@
+"""The C ABI library loads and exports every symbol include/tfb200.h declares.
+
+CPU only: calls here are restricted to those that never touch a device
+(version, workspace sizing, host-side argument validation).
+"""
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "tfb200.h"
+
+
+@pytest.fixture(scope="module")
+def L():
+    from tfb200 import _lib
+
+    if not _lib.LIB_PATH.exists():
+        subprocess.run(["make", "-C", str(_lib.PKG_ROOT)], check=True, capture_output=True)
+    return _lib
+
+
+def declared():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(tfb200_\w+)\s*\(", text, re.M)))
+
+
+def test_header_lists_the_binding_exports(L):
+    assert declared() == sorted(L.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol(L):
+    lib = ctypes.CDLL(str(L.LIB_PATH))
+    for name in declared():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(L.LIB_PATH)], capture_output=True, text=True).stdout
+    for name in declared():
+        assert re.search(rf"\bT {name}$", out, re.M), name
+
+
+def test_version_and_workspace(L):
+    lib = L.lib()
+    assert lib.tfb200_version() == 1
+    assert lib.tfb200_fused_mlp_workspace_size(8192, 4096, 16384, 4096) == 8192 * 16384 * 2
+    assert lib.tfb200_fused_mlp_workspace_size(0, 4096, 16384, 4096) == 0
+    assert lib.tfb200_fused_mlp_workspace_size(3, 8, 5, 8) == 256
+
+
+def test_host_validation_needs_no_device(L):
+    lib = L.lib()
+    a = L.Mat(None, 4, 8, 8, L.TFB200_BF16)
+    b = L.Mat(None, 9, 8, 8, L.TFB200_BF16)  # inner dims disagree
+    c = L.Mat(None, 4, 8, 8, L.TFB200_BF16)
+    assert lib.tfb200_matmul(ctypes.byref(a), ctypes.byref(b), ctypes.byref(c), None) == L.TFB200_EINVAL
+    assert b"null data" in lib.tfb200_last_error() or b"shapes" in lib.tfb200_last_error()
+    bad = L.Mat(None, 4, 8, 4, L.TFB200_BF16)  # ld < cols
+    assert lib.tfb200_matmul(ctypes.byref(bad), ctypes.byref(a), ctypes.byref(c), None) == L.TFB200_EINVAL
+    f32 = L.Mat(None, 4, 8, 8, L.TFB200_F32)
+    assert lib.tfb200_matmul(ctypes.byref(f32), ctypes.byref(a), ctypes.byref(c), None) == L.TFB200_EINVAL
+    assert lib.tfb200_fused_mlp(None, None, None, None, None, None, 1e-5, 0, None, None, None, 0) == L.TFB200_EINVAL

@@ -1,0 +1,191 @@
+"""Parity of the sm_100a kernels (through the C ABI) against the oracle.
+
+Small workloads are compared over the whole output with the reference's own
+golden output (fixtures); the full-size workloads are compared row by row on a
+sample of rows (each output row depends only on its input row), against the
+fixtures' rows and against the oracle on further rows. Bar: max |y - golden| /
+rms(golden) <= 2e-2 and PCC >= 0.9999 (tfb200.metrics), with non-vacuity checks:
+the output is bf16 and differs from the fp32 golden.
+"""
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import golden as O  # noqa: E402
+from tfb200 import workloads as W  # noqa: E402
+from tfb200.metrics import parity  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+f32 = W.bf16_to_f32
+
+
+def dev(a: np.ndarray):
+    """uint16 bf16 encodings -> CUDA bf16 tensor."""
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda().view(torch.bfloat16)
+
+
+def host(t) -> np.ndarray:
+    return t.float().cpu().numpy()
+
+
+@pytest.fixture(scope="module")
+def ops():
+    assert torch.cuda.is_available(), "parity tests need a CUDA device"
+    from tfb200 import ops as _ops
+
+    return _ops
+
+
+def assert_parity(got, golden, what):
+    m = parity(got, golden)
+    assert m["ok"], f"{what}: {m}"
+    assert np.array_equal(O.to_bf16(got), got), f"{what}: output is not bf16"
+    assert m["max_abs_diff"] > 0, f"{what}: output equals the fp32 golden bit for bit (vacuous)"
+    return m
+
+
+def test_rmsnorm_matmul_small_vs_reference(ops, golden_vectors):
+    t = W.generate("rmsnorm_matmul_small")
+    y = ops.fused_rmsnorm_matmul(dev(t["x"]), dev(t["gamma"]), dev(t["w"]), 1e-5)
+    assert_parity(host(y), golden_vectors["rmsnorm_matmul_small/golden"], "rmsnorm_matmul_small")
+
+
+def test_matmul_256x512x1024_vs_reference(ops, golden_vectors):
+    t = W.generate("matmul_256x512x1024")
+    y = host(ops.matmul(dev(t["a"]), dev(t["b"])))
+    rows = golden_vectors["matmul_256x512x1024/rows"]
+    assert_parity(y[rows], golden_vectors["matmul_256x512x1024/golden"], "matmul rows")
+    assert_parity(y, O.matmul(f32(t["a"]), f32(t["b"])), "matmul full")
+
+
+def test_matmul_padded_vs_reference(ops, golden_vectors):
+    """100x50x100: row strides of 100 and 200 bytes, which TMA cannot describe."""
+    t = W.generate("matmul_padded")
+    y = host(ops.matmul(dev(t["a"]), dev(t["b"])))
+    assert_parity(y, golden_vectors["matmul_padded/golden"], "matmul_padded")
+
+
+@pytest.mark.parametrize("gelu", ["erf", "tanh"])
+def test_mlp_block_small(ops, golden_vectors, gelu):
+    t = W.generate("mlp_block_small")
+    x = dev(t["x"])
+    y = host(ops.fused_mlp(x, dev(t["gamma"]), dev(t["w1"]), dev(t["b1"]), dev(t["w2"]), x, 1e-5, gelu=gelu))
+    if gelu == "erf":
+        g = golden_vectors["mlp_block_small/golden"]
+    else:
+        xf = f32(t["x"])
+        g = O.fused_mlp(xf, f32(t["gamma"]), f32(t["w1"]), f32(t["b1"]), f32(t["w2"]), xf, 1e-5, "tanh")
+    assert_parity(y, g, f"mlp_block_small/{gelu}")
+
+
+RAGGED = [(1, 64, 8), (200, 136, 300), (129, 64, 257), (300, 520, 40), (64, 4096, 1000)]
+
+
+@pytest.mark.parametrize("m,k,n", RAGGED)
+def test_fused_rmsnorm_matmul_ragged(ops, m, k, n):
+    rng = np.random.default_rng(m * 7 + k * 3 + n)
+    x = W.bf16_bits(rng.standard_normal((m, k), dtype=np.float32))
+    g = W.bf16_bits(0.5 + rng.random(k, dtype=np.float32))
+    w = W.bf16_bits(rng.standard_normal((k, n), dtype=np.float32) / np.float32(np.sqrt(k)))
+    y = host(ops.fused_rmsnorm_matmul(dev(x), dev(g), dev(w), 1e-5))
+    assert_parity(y, O.fused_rmsnorm_matmul(f32(x), f32(g), f32(w), 1e-5), f"ragged {m}x{k}x{n}")
+
+
+@pytest.mark.parametrize("m,k,n", [(3, 5, 7), (100, 50, 100), (130, 72, 260), (257, 64, 64)])
+def test_matmul_ragged(ops, m, k, n):
+    rng = np.random.default_rng(m + k + n)
+    a = W.bf16_bits(rng.standard_normal((m, k), dtype=np.float32))
+    b = W.bf16_bits(rng.standard_normal((k, n), dtype=np.float32) / np.float32(np.sqrt(k)))
+    y = host(ops.matmul(dev(a), dev(b)))
+    assert_parity(y, O.matmul(f32(a), f32(b)), f"matmul {m}x{k}x{n}")
+
+
+def test_strided_views_and_leading_dims(ops):
+    """ld > cols for every operand, and a 3-D activation flattened to rows."""
+    rng = np.random.default_rng(11)
+    big_x = dev(W.bf16_bits(rng.standard_normal((2, 96, 200), dtype=np.float32)))
+    x = big_x[:, :, :128]                     # [2, 96, 128], row stride 200
+    g = dev(W.bf16_bits(0.5 + rng.random(128, dtype=np.float32)))
+    big_w = dev(W.bf16_bits(rng.standard_normal((128, 400), dtype=np.float32) / np.float32(np.sqrt(128))))
+    w = big_w[:, :264]
+    y = ops.fused_rmsnorm_matmul(x, g, w, 1e-5)
+    assert tuple(y.shape) == (2, 96, 264)
+    xf = host(x).reshape(-1, 128)
+    golden = O.fused_rmsnorm_matmul(xf, host(g), host(w), 1e-5)
+    assert_parity(host(y).reshape(-1, 264), golden, "strided")
+    out_big = torch.zeros(192, 300, dtype=torch.bfloat16, device="cuda")
+    ops.fused_rmsnorm_matmul(x.reshape(-1, 128), g, w, 1e-5, out=out_big[:, :264])
+    assert_parity(host(out_big[:, :264]), golden, "strided out")
+    assert torch.count_nonzero(out_big[:, 264:]).item() == 0, "wrote outside the output view"
+
+
+def test_matmul_k_zero_gives_zeros(ops):
+    a = torch.empty(5, 0, dtype=torch.bfloat16, device="cuda")
+    b = torch.empty(0, 7, dtype=torch.bfloat16, device="cuda")
+    y = ops.matmul(a, b)
+    assert tuple(y.shape) == (5, 7) and torch.count_nonzero(y).item() == 0
+
+
+def test_empty_rows_is_noop(ops):
+    x = torch.empty(0, 64, dtype=torch.bfloat16, device="cuda")
+    g = torch.ones(64, dtype=torch.bfloat16, device="cuda")
+    w = torch.ones(64, 32, dtype=torch.bfloat16, device="cuda")
+    assert tuple(ops.fused_rmsnorm_matmul(x, g, w).shape) == (0, 32)
+
+
+def test_errors_are_loud(ops):
+    from tfb200._lib import TFB200Error
+
+    x = torch.ones(4, 64, dtype=torch.bfloat16, device="cuda")
+    g = torch.ones(64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        ops.fused_rmsnorm_matmul(x, g, torch.ones(63, 8, dtype=torch.bfloat16, device="cuda"))
+    with pytest.raises(ValueError):
+        ops.fused_rmsnorm_matmul(x, torch.ones(32, dtype=torch.bfloat16, device="cuda"),
+                                 torch.ones(64, 8, dtype=torch.bfloat16, device="cuda"))
+    with pytest.raises(TypeError):
+        ops.matmul(x.float(), torch.ones(64, 8, device="cuda"))
+    x5 = torch.ones(4, 60, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(TFB200Error):  # K % 8 != 0 is refused by the fused path
+        ops.fused_rmsnorm_matmul(x5, torch.ones(60, dtype=torch.bfloat16, device="cuda"),
+                                 torch.ones(60, 8, dtype=torch.bfloat16, device="cuda"))
+
+
+# ------------------------------------------------------------ full-size workloads
+
+
+def _sample_rows(m, fixture_rows, n_extra, seed):
+    rng = np.random.default_rng(seed)
+    extra = rng.choice(m, size=min(n_extra, m), replace=False)
+    return np.unique(np.concatenate([fixture_rows, extra]))
+
+
+def test_qkv_full_size(ops, golden_vectors):
+    name = "qkv_8192x4096x6144"
+    t = W.generate(name)
+    y = host(ops.fused_rmsnorm_matmul(dev(t["x"]), dev(t["gamma"]), dev(t["w"]), 1e-5))
+    fr = golden_vectors[f"{name}/rows"]
+    assert_parity(y[fr], golden_vectors[f"{name}/golden"], "qkv fixture rows")
+    rows = _sample_rows(8192, fr, 60, 1)
+    g = O.fused_rmsnorm_matmul(f32(t["x"][rows]), f32(t["gamma"]), f32(t["w"]), 1e-5)
+    assert_parity(y[rows], g, "qkv sampled rows")
+    assert np.all(np.isfinite(y))
+
+
+@pytest.mark.parametrize("name", ["mlp_8192x4096x16384", "decode_mlp_32x8192x28672"])
+def test_mlp_full_size(ops, golden_vectors, name):
+    t = W.generate(name)
+    x = dev(t["x"])
+    args = (x, dev(t["gamma"]), dev(t["w1"]), dev(t["b1"]), dev(t["w2"]), x, 1e-5)
+    fr = golden_vectors[f"{name}/rows"]
+    y = host(ops.fused_mlp(*args, gelu="erf"))
+    assert_parity(y[fr], golden_vectors[f"{name}/golden"], f"{name} erf fixture rows")
+    yt = host(ops.fused_mlp(*args, gelu="tanh"))
+    rows = _sample_rows(t["x"].shape[0], fr, 28, 2)
+    xs = f32(t["x"][rows])
+    g = O.fused_mlp(xs, f32(t["gamma"]), f32(t["w1"]), f32(t["b1"]), f32(t["w2"]), xs, 1e-5, "tanh")
+    assert_parity(yt[rows], g, f"{name} tanh sampled rows")
+    assert np.all(np.isfinite(y)) and np.all(np.isfinite(yt))

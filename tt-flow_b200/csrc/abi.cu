@@ -1,0 +1,266 @@
+// C ABI of libtfb200 (declared in include/tfb200.h): argument validation, error
+// reporting and dispatch to the sm_100a kernels.
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/tfb200.h"
+#include "internal.h"
+#include "sm100_ptx.cuh"
+
+namespace tfb200 {
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
+std::atomic<uint64_t> g_wait_ns{2000000000ull};
+
+// Per-device status word written by kernels whose bounded waits ran out.
+__device__ int g_device_status;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+__global__ void k_fill_zero_bf16(bf16* c, int64_t rows, int64_t cols, int64_t ld) {
+  const int64_t n = rows * cols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols, cc = i - r * cols;
+    c[r * ld + cc] = __float2bfloat16_rn(0.0f);
+  }
+}
+
+bool mat_ok(const tfb200_mat* m, const char* name, std::string* err) {
+  if (!m) {
+    *err = std::string(name) + ": null descriptor";
+    return false;
+  }
+  if (m->dtype != TFB200_BF16) {
+    *err = std::string(name) + ": dtype must be TFB200_BF16";
+    return false;
+  }
+  if (m->rows < 0 || m->cols < 0) {
+    *err = std::string(name) + ": negative shape";
+    return false;
+  }
+  if (m->ld < m->cols || m->ld < 1) {
+    *err = std::string(name) + ": leading dimension smaller than the column count";
+    return false;
+  }
+  if (!m->data && m->rows > 0 && m->cols > 0) {
+    *err = std::string(name) + ": null data";
+    return false;
+  }
+  return true;
+}
+
+const bf16* as_bf16(const void* p) { return static_cast<const bf16*>(p); }
+
+}  // namespace
+
+int* device_status_ptr(std::string* err) {
+  static int* ptrs[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    if (err) *err = "no current CUDA device";
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_device_status);
+    if (e != cudaSuccess) {
+      if (err) *err = std::string("cudaGetSymbolAddress(status): ") + cudaGetErrorString(e);
+      return nullptr;
+    }
+    ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+int sm_count() {
+  static int counts[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!counts[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    counts[dev] = n > 0 ? n : 148;
+  }
+  return counts[dev];
+}
+
+uint64_t launches() { return g_launches.load(); }
+void count_launch(uint64_t n) { g_launches.fetch_add(n); }
+uint64_t wait_limit_ns() { return g_wait_ns.load(); }
+void set_wait_limit_ns(uint64_t ns) { g_wait_ns.store(ns ? ns : 1); }
+
+}  // namespace tfb200
+
+using namespace tfb200;
+
+extern "C" {
+
+int tfb200_version(void) { return TFB200_ABI_VERSION; }
+
+const char* tfb200_last_error(void) { return g_last_error.c_str(); }
+
+uint64_t tfb200_launch_count(void) { return launches(); }
+
+void tfb200_set_wait_limit_ns(uint64_t ns) { set_wait_limit_ns(ns); }
+
+int tfb200_device_status(void) {
+  std::string err;
+  int* p = device_status_ptr(&err);
+  if (!p) return fail(TFB200_ECUDA, err);
+  int v = 0;
+  cudaError_t e = cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(TFB200_ECUDA, std::string("status read: ") + cudaGetErrorString(e));
+  return v == kDevOk ? TFB200_OK : TFB200_ETIMEOUT;
+}
+
+int tfb200_clear_device_status(void) {
+  std::string err;
+  int* p = device_status_ptr(&err);
+  if (!p) return fail(TFB200_ECUDA, err);
+  int zero = 0;
+  cudaError_t e = cudaMemcpy(p, &zero, sizeof(int), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return fail(TFB200_ECUDA, std::string("status clear: ") + cudaGetErrorString(e));
+  return TFB200_OK;
+}
+
+int tfb200_matmul(const tfb200_mat* a, const tfb200_mat* b, tfb200_mat* c, void* stream) {
+  std::string err;
+  if (!mat_ok(a, "a", &err) || !mat_ok(b, "b", &err) || !mat_ok(c, "c", &err))
+    return fail(TFB200_EINVAL, "tfb200_matmul: " + err);
+  if (a->cols != b->rows || c->rows != a->rows || c->cols != b->cols)
+    return fail(TFB200_EINVAL, "tfb200_matmul: shapes do not agree (A[M,K] @ B[K,N] -> C[M,N])");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (c->rows == 0 || c->cols == 0) return TFB200_OK;
+  if (a->cols == 0) {
+    const int64_t n = c->rows * c->cols;
+    const int blocks = static_cast<int>(n / 256 + 1 < 4096 ? n / 256 + 1 : 4096);
+    k_fill_zero_bf16<<<blocks, 256, 0, s>>>(static_cast<bf16*>(c->data), c->rows, c->cols, c->ld);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(TFB200_ECUDA, std::string("tfb200_matmul: ") + cudaGetErrorString(e));
+    count_launch();
+    return TFB200_OK;
+  }
+  GemmProblem g;
+  g.M = a->rows;
+  g.N = b->cols;
+  g.K = a->cols;
+  g.A = as_bf16(a->data);
+  g.lda = a->ld;
+  g.B = as_bf16(b->data);
+  g.ldb = b->ld;
+  g.C = static_cast<bf16*>(c->data);
+  g.ldc = c->ld;
+  int rc = run_gemm(g, s, &err);
+  return rc ? fail(rc, "tfb200_matmul: " + err) : TFB200_OK;
+}
+
+int tfb200_fused_rmsnorm_matmul(const tfb200_mat* x, const void* gamma, const tfb200_mat* w, float eps,
+                                tfb200_mat* y, void* stream) {
+  std::string err;
+  if (!mat_ok(x, "x", &err) || !mat_ok(w, "w", &err) || !mat_ok(y, "y", &err))
+    return fail(TFB200_EINVAL, "tfb200_fused_rmsnorm_matmul: " + err);
+  if (x->cols != w->rows || y->rows != x->rows || y->cols != w->cols)
+    return fail(TFB200_EINVAL, "tfb200_fused_rmsnorm_matmul: shapes do not agree (X[M,K], W[K,N] -> Y[M,N])");
+  if (!(eps >= 0.0f)) return fail(TFB200_EINVAL, "tfb200_fused_rmsnorm_matmul: eps must be >= 0");
+  if (y->rows == 0 || y->cols == 0) return TFB200_OK;
+  if (x->cols == 0) return fail(TFB200_EINVAL, "tfb200_fused_rmsnorm_matmul: RMSNorm over an empty dimension");
+  if (!gamma) return fail(TFB200_EINVAL, "tfb200_fused_rmsnorm_matmul: null gamma");
+  if (x->cols % 8 != 0)
+    return fail(TFB200_EUNSUPPORTED, "tfb200_fused_rmsnorm_matmul: K must be a multiple of 8");
+  GemmProblem g;
+  g.M = x->rows;
+  g.N = w->cols;
+  g.K = x->cols;
+  g.A = as_bf16(x->data);
+  g.lda = x->ld;
+  g.B = as_bf16(w->data);
+  g.ldb = w->ld;
+  g.C = static_cast<bf16*>(y->data);
+  g.ldc = y->ld;
+  g.gamma = as_bf16(gamma);
+  g.eps = eps;
+  int rc = run_gemm(g, static_cast<cudaStream_t>(stream), &err);
+  return rc ? fail(rc, "tfb200_fused_rmsnorm_matmul: " + err) : TFB200_OK;
+}
+
+size_t tfb200_fused_mlp_workspace_size(int64_t m, int64_t k, int64_t h, int64_t n) {
+  (void)k;
+  (void)n;
+  if (m <= 0 || h <= 0) return 0;
+  const size_t bytes = static_cast<size_t>(m) * static_cast<size_t>(h) * 2;
+  return (bytes + 255) & ~static_cast<size_t>(255);
+}
+
+int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w1, const void* b1,
+                     const tfb200_mat* w2, const tfb200_mat* residual, float eps, int gelu_mode, tfb200_mat* y,
+                     void* stream, void* workspace, size_t workspace_bytes) {
+  std::string err;
+  if (!mat_ok(x, "x", &err) || !mat_ok(w1, "w1", &err) || !mat_ok(w2, "w2", &err) ||
+      !mat_ok(residual, "residual", &err) || !mat_ok(y, "y", &err))
+    return fail(TFB200_EINVAL, "tfb200_fused_mlp: " + err);
+  const int64_t M = x->rows, K = x->cols, H = w1->cols, N = w2->cols;
+  if (w1->rows != K || w2->rows != H || y->rows != M || y->cols != N || residual->rows != M ||
+      residual->cols != N)
+    return fail(TFB200_EINVAL,
+                "tfb200_fused_mlp: shapes do not agree (X[M,K], W1[K,H], W2[H,N], R[M,N] -> Y[M,N])");
+  if (gelu_mode != TFB200_GELU_ERF && gelu_mode != TFB200_GELU_TANH)
+    return fail(TFB200_EINVAL, "tfb200_fused_mlp: gelu_mode must be TFB200_GELU_ERF or TFB200_GELU_TANH");
+  if (!(eps >= 0.0f)) return fail(TFB200_EINVAL, "tfb200_fused_mlp: eps must be >= 0");
+  if (M == 0 || N == 0) return TFB200_OK;
+  if (K == 0) return fail(TFB200_EINVAL, "tfb200_fused_mlp: RMSNorm over an empty dimension");
+  if (!gamma) return fail(TFB200_EINVAL, "tfb200_fused_mlp: null gamma");
+  if (K % 8 != 0) return fail(TFB200_EUNSUPPORTED, "tfb200_fused_mlp: K must be a multiple of 8");
+  if (H == 0) return fail(TFB200_EUNSUPPORTED, "tfb200_fused_mlp: empty hidden dimension");
+  const size_t need = tfb200_fused_mlp_workspace_size(M, K, H, N);
+  if (!workspace || workspace_bytes < need)
+    return fail(TFB200_EWORKSPACE, "tfb200_fused_mlp: workspace smaller than tfb200_fused_mlp_workspace_size()");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+    return fail(TFB200_EWORKSPACE, "tfb200_fused_mlp: workspace must be 256-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  bf16* hid = static_cast<bf16*>(workspace);
+  GemmProblem g1;
+  g1.M = M;
+  g1.N = H;
+  g1.K = K;
+  g1.A = as_bf16(x->data);
+  g1.lda = x->ld;
+  g1.B = as_bf16(w1->data);
+  g1.ldb = w1->ld;
+  g1.C = hid;
+  g1.ldc = H;
+  g1.gamma = as_bf16(gamma);
+  g1.eps = eps;
+  g1.bias = as_bf16(b1);
+  g1.gelu = gelu_mode == TFB200_GELU_ERF ? kGeluErf : kGeluTanh;
+  int rc = run_gemm(g1, s, &err);
+  if (rc) return fail(rc, "tfb200_fused_mlp (up projection): " + err);
+  GemmProblem g2;
+  g2.M = M;
+  g2.N = N;
+  g2.K = H;
+  g2.A = hid;
+  g2.lda = H;
+  g2.B = as_bf16(w2->data);
+  g2.ldb = w2->ld;
+  g2.C = static_cast<bf16*>(y->data);
+  g2.ldc = y->ld;
+  g2.residual = as_bf16(residual->data);
+  g2.ldr = residual->ld;
+  rc = run_gemm(g2, s, &err);
+  if (rc) return fail(rc, "tfb200_fused_mlp (down projection): " + err);
+  return TFB200_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,585 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a with the fused RMSNorm
+// prologue and the bias / GELU / residual epilogue of the tt-flow hot path.
+//
+// This replaces the Tensix compute kernels that the reference emits as strings:
+// the fused RMSNorm+MatMul compute (tensixflow lib/tensixflow/Codegen/
+// EmitCompute.cpp:60-255), the fused MLP compute (:331-558) and the plain tiled
+// matmul compute (:257-329, :560-650), together with their reader and writer
+// kernels (EmitReader.cpp, EmitWriter.cpp).
+//
+// One CTA per SM walks output tiles of 128 x 256 (grid-stride over a grouped
+// raster so that concurrently running tiles share A and B panels in L2).
+// Warp roles:
+//   warp 0      TMA producer: A tile [128 x 64] (K-major) and B tile [64 x 256]
+//               (N-major, four 64-column boxes), 128-byte swizzle, S stages.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma 128x256x16 into a
+//               double-buffered fp32 accumulator in TMEM (2 x 256 columns).
+//   warp 2      TMEM allocator.
+//   warps 4-7   epilogue: tcgen05.ld 32 columns at a time, row scale, bias,
+//               GELU, residual, bf16 round, store.
+//   warps 8-11  RMSNorm prologue (only when gamma is given): thread r owns row r
+//               of each A stage, accumulates sum(x^2) in fp32, rewrites the stage
+//               in place as bf16(x * gamma) and hands it to the MMA warp; at the
+//               end of the K loop it publishes 1/sqrt(sum/K + eps) for the
+//               epilogue's row scale. rmsnorm(x) @ W = diag(1/rms) (x*gamma) @ W,
+//               so the activation is read from HBM once.
+//   warps 12-15 (only for operands TMA cannot describe: leading dimensions that
+//               are not multiples of 8 elements or unaligned pointers) plain-load
+//               producer that writes the same swizzled stage layout.
+// Every wait is bounded; when one runs out the kernel records kDevTimeout in the
+// device status word, drains what it issued and returns.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "internal.h"
+#include "sm100_ptx.cuh"
+
+namespace tfb200 {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr uint32_t A_STAGE_BYTES = BM * BK * 2;  // 16 KiB
+constexpr uint32_t B_STAGE_BYTES = BN * BK * 2;  // 32 KiB
+constexpr uint32_t TMEM_COLS = 2 * BN;           // two accumulators
+constexpr int GROUP_M = 16;                      // raster group (tiles of M)
+
+struct KParams {
+  int M, N, K;
+  const bf16* A;
+  int64_t lda;
+  const bf16* B;
+  int64_t ldb;
+  bf16* C;
+  int64_t ldc;
+  const bf16* gamma;
+  float eps;
+  const bf16* bias;
+  int gelu;
+  const bf16* residual;
+  int64_t ldr;
+  int vec_ok;  // C / residual / bias allow 16-byte accesses
+  int* status;
+  uint64_t timeout_ns;
+};
+
+struct SmemCtl {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t xfull[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t ifull[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  float inv[2][BM];
+};
+
+constexpr size_t smem_bytes() {
+  return 1024 /*alignment slack*/ + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + sizeof(SmemCtl);
+}
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm, int& tn) {
+  const int per_group = GROUP_M * num_n;
+  const int g = t / per_group;
+  const int first_m = g * GROUP_M;
+  const int gsize = min(num_m - first_m, GROUP_M);
+  const int local = t - g * per_group;
+  tm = first_m + local % gsize;
+  tn = local / gsize;
+}
+
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.0f + tanhf(u));
+}
+
+__device__ __forceinline__ void raise_abort(SmemCtl* ctl, int* status) {
+  ctl->abort = 1;
+  atomicExch(status, kDevTimeout);
+}
+
+// Warp-uniform bounded wait (every lane waits; the warp agrees on the outcome).
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, SmemCtl* ctl, const KParams& p) {
+  bool ok = mbar_wait(bar, parity, &ctl->abort, p.timeout_ns);
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok && (threadIdx.x & 31) == 0) raise_abort(ctl, p.status);
+  return ok;
+}
+
+template <bool RMS, bool MANUAL>
+__global__ void __launch_bounds__(256 + (RMS ? 128 : 0) + (MANUAL ? 128 : 0), 1)
+    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const KParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
+  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(sB + STAGES * B_STAGE_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  constexpr int kXformWarp0 = 8;
+  constexpr int kLoadWarp0 = RMS ? 12 : 8;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&ctl->full[s]), MANUAL ? 128 : 1);
+      mbar_init(smem_u32(&ctl->empty[s]), 1);
+      mbar_init(smem_u32(&ctl->xfull[s]), 128);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&ctl->tfull[b]), 1);
+      mbar_init(smem_u32(&ctl->tempty[b]), 128);
+      mbar_init(smem_u32(&ctl->ifull[b]), 128);
+    }
+    mbar_init(smem_u32(&ctl->drain), 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+    if (!MANUAL) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+    }
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = ctl->tmem_base;
+
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int total = num_m * num_n;
+  const int kblocks = (p.K + BK - 1) / BK;
+
+  if (warp == 0 && !MANUAL) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0, armed_phase = 0;  // stages with loads in flight (for the drain)
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, num_m, num_n, tm, tn);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(smem_u32(&ctl->empty[stage]), phase ^ 1u, &ctl->abort, p.timeout_ns)) {
+            raise_abort(ctl, p.status);
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&ctl->full[stage]);
+          mbar_arrive_expect_tx(fb, A_STAGE_BYTES + B_STAGE_BYTES);
+          tma_load_2d(smem_u32(sA + stage * A_STAGE_BYTES), &tmA, fb, kb * BK, tm * BM);
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_2d(smem_u32(sB + stage * B_STAGE_BYTES + j * 8192), &tmB, fb, tn * BN + j * 64, kb * BK);
+          armed |= 1u << stage;
+          armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the copies already issued land before the CTA's shared memory goes away.
+        for (int s = 0; s < STAGES; ++s)
+          if (armed & (1u << s)) {
+            const uint64_t t0 = global_ns();
+            while (!mbar_test(smem_u32(&ctl->full[s]), (armed_phase >> s) & 1u) &&
+                   global_ns() - t0 < p.timeout_ns) {
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(BM, BN, false, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int i = 0;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++i) {
+        const int acc = i & 1;
+        const uint32_t use = static_cast<uint32_t>(i >> 1);
+        if (!mbar_wait(smem_u32(&ctl->tempty[acc]), (use & 1u) ^ 1u, &ctl->abort, p.timeout_ns)) {
+          raise_abort(ctl, p.status);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          const uint32_t wb = RMS ? smem_u32(&ctl->xfull[stage]) : smem_u32(&ctl->full[stage]);
+          if (!mbar_wait(wb, phase, &ctl->abort, p.timeout_ns)) {
+            raise_abort(ctl, p.status);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_STAGE_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * B_STAGE_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b0 + k * 2048, 8192, 1024);
+            mma_bf16(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(smem_u32(&ctl->empty[stage]));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) mma_commit(smem_u32(&ctl->tfull[acc]));
+      }
+      // Wait until every MMA this thread issued has finished (TMEM is freed below).
+      mma_commit(smem_u32(&ctl->drain));
+      const uint64_t t0 = global_ns();
+      while (!mbar_test(smem_u32(&ctl->drain), 0) && global_ns() - t0 < p.timeout_ns) {
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int r = q * 32 + lane;
+    int i = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
+      int tm, tn;
+      tile_coords(t, num_m, num_n, tm, tn);
+      const int acc = i & 1;
+      const uint32_t use = static_cast<uint32_t>(i >> 1);
+      if (!warp_wait(smem_u32(&ctl->tfull[acc]), use & 1u, ctl, p)) break;
+      if (RMS && !warp_wait(smem_u32(&ctl->ifull[acc]), use & 1u, ctl, p)) break;
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(tm) * BM + r;
+      const float scale = RMS ? ctl->inv[acc][r] : 1.0f;
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = tn * BN + c * 32;
+        if (col0 >= p.N) break;  // warp-uniform
+        uint32_t v[32];
+        tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + c * 32),
+                       v);
+        tmem_wait_ld();
+        if (row < p.M) {
+          float f[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * scale;
+          const bool full = p.vec_ok && (col0 + 32 <= p.N);
+          if (p.bias) {
+            if (full) {
+              const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0);
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const uint4 b = __ldg(bp + u);
+                const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  f[u * 8 + 2 * e] += bf16_lo(bw[e]);
+                  f[u * 8 + 2 * e + 1] += bf16_hi(bw[e]);
+                }
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) f[j] += __bfloat162float(p.bias[col0 + j]);
+            }
+          }
+          if (p.gelu == kGeluErf) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[j] = gelu_erf(f[j]);
+          } else if (p.gelu == kGeluTanh) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[j] = gelu_tanh(f[j]);
+          }
+          if (p.residual) {
+            const bf16* rp = p.residual + row * p.ldr + col0;
+            if (full) {
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const uint4 b = *reinterpret_cast<const uint4*>(rp + u * 8);
+                const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  f[u * 8 + 2 * e] += bf16_lo(bw[e]);
+                  f[u * 8 + 2 * e + 1] += bf16_hi(bw[e]);
+                }
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) f[j] += __bfloat162float(rp[j]);
+            }
+          }
+          bf16* cp = p.C + row * p.ldc + col0;
+          if (full) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              uint4 o;
+              o.x = pack_bf16(f[u * 8 + 0], f[u * 8 + 1]);
+              o.y = pack_bf16(f[u * 8 + 2], f[u * 8 + 3]);
+              o.z = pack_bf16(f[u * 8 + 4], f[u * 8 + 5]);
+              o.w = pack_bf16(f[u * 8 + 6], f[u * 8 + 7]);
+              *reinterpret_cast<uint4*>(cp + u * 8) = o;
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N) cp[j] = __float2bfloat16_rn(f[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&ctl->tempty[acc]));
+    }
+  } else if (RMS && warp >= kXformWarp0 && warp < kXformWarp0 + 4) {
+    // -------------------------------------------------------- RMSNorm prologue
+    const int r = threadIdx.x - kXformWarp0 * 32;  // row within the tile
+    int stage = 0;
+    uint32_t phase = 0;
+    int i = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++i) {
+      const int acc = i & 1;
+      const uint32_t use = static_cast<uint32_t>(i >> 1);
+      float ss = 0.0f;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!warp_wait(smem_u32(&ctl->full[stage]), phase, ctl, p)) {
+          ok = false;
+          break;
+        }
+        uint8_t* rowp = sA + stage * A_STAGE_BYTES + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int k0 = kb * BK + c * 8;
+          uint4* cp = reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4));
+          const uint4 xv = *cp;
+          uint4 gv = make_uint4(0u, 0u, 0u, 0u);
+          if (k0 < p.K) gv = __ldg(reinterpret_cast<const uint4*>(p.gamma + k0));
+          const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+          uint32_t ow[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float x0 = bf16_lo(xw[e]), x1 = bf16_hi(xw[e]);
+            ss = fmaf(x0, x0, ss);
+            ss = fmaf(x1, x1, ss);
+            ow[e] = pack_bf16(x0 * bf16_lo(gw[e]), x1 * bf16_hi(gw[e]));
+          }
+          *cp = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        }
+        fence_proxy_async_smem();
+        if (kb == kblocks - 1) {
+          // The epilogue of the tile that last used this slot must be done with it.
+          if (!warp_wait(smem_u32(&ctl->tempty[acc]), (use & 1u) ^ 1u, ctl, p)) {
+            ok = false;
+            break;
+          }
+          ctl->inv[acc][r] = 1.0f / sqrtf(ss / static_cast<float>(p.K) + p.eps);
+          mbar_arrive(smem_u32(&ctl->ifull[acc]));
+        }
+        mbar_arrive(smem_u32(&ctl->xfull[stage]));
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (MANUAL && warp >= kLoadWarp0 && warp < kLoadWarp0 + 4) {
+    // ------------------------------------------------- plain-load producer
+    const int tid = threadIdx.x - kLoadWarp0 * 32;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(t, num_m, num_n, tm, tn);
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!warp_wait(smem_u32(&ctl->empty[stage]), phase ^ 1u, ctl, p)) {
+          ok = false;
+          break;
+        }
+        // A: thread tid owns row tid of the tile.
+        {
+          const int64_t gm = static_cast<int64_t>(tm) * BM + tid;
+          uint8_t* rowp = sA + stage * A_STAGE_BYTES + tid * 128;
+          for (int c = 0; c < 8; ++c) {
+            uint32_t w[4];
+            for (int e = 0; e < 4; ++e) {
+              const int k = kb * BK + c * 8 + 2 * e;
+              float lo = 0.f, hi = 0.f;
+              if (gm < p.M && k < p.K) lo = __bfloat162float(p.A[gm * p.lda + k]);
+              if (gm < p.M && k + 1 < p.K) hi = __bfloat162float(p.A[gm * p.lda + k + 1]);
+              w[e] = pack_bf16(lo, hi);
+            }
+            *reinterpret_cast<uint4*>(rowp + ((c ^ (tid & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+        // B: thread tid owns k-row tid/2 and 128 of the 256 columns.
+        {
+          const int kr = tid >> 1;
+          const int64_t gk = static_cast<int64_t>(kb) * BK + kr;
+          for (int cc = 0; cc < 16; ++cc) {
+            const int nl = (tid & 1) * 128 + cc * 8;
+            uint32_t w[4];
+            for (int e = 0; e < 4; ++e) {
+              const int64_t n = static_cast<int64_t>(tn) * BN + nl + 2 * e;
+              float lo = 0.f, hi = 0.f;
+              if (gk < p.K && n < p.N) lo = __bfloat162float(p.B[gk * p.ldb + n]);
+              if (gk < p.K && n + 1 < p.N) hi = __bfloat162float(p.B[gk * p.ldb + n + 1]);
+              w[e] = pack_bf16(lo, hi);
+            }
+            uint8_t* dst = sB + stage * B_STAGE_BYTES + (nl >> 6) * 8192 + kr * 128 +
+                           ((((nl & 63) >> 3) ^ (kr & 7)) << 4);
+            *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(smem_u32(&ctl->full[stage]));
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn(std::string* err) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  if (!fn && err) *err = "cuTensorMapEncodeTiled is unavailable from the CUDA driver";
+  return fn;
+}
+
+// Row-major bf16 matrix [rows, cols] with leading dimension ld: box of
+// 64 (cols) x box_rows, 128-byte swizzle, zero fill outside the matrix.
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, uint32_t box_rows,
+              std::string* err) {
+  auto fn = encode_fn(err);
+  if (!fn) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    if (err) *err = "cuTensorMapEncodeTiled failed (CUresult " + std::to_string(static_cast<int>(r)) + ")";
+    return false;
+  }
+  return true;
+}
+
+template <bool RMS, bool MANUAL>
+int launch(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int grid, cudaStream_t s,
+           std::string* err) {
+  auto kern = k_gemm<RMS, MANUAL>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const size_t smem = smem_bytes();
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) {
+      if (err) *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+      return -3;
+    }
+    attr_set[dev] = true;
+  }
+  constexpr int threads = 256 + (RMS ? 128 : 0) + (MANUAL ? 128 : 0);
+  kern<<<grid, threads, smem, s>>>(ta, tb, kp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    if (err) *err = std::string("gemm launch: ") + cudaGetErrorString(e);
+    return -3;
+  }
+  count_launch();
+  return 0;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int run_gemm(const GemmProblem& g, cudaStream_t stream, std::string* err) {
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0) {
+    if (err) *err = "run_gemm: empty problem";
+    return -1;
+  }
+  if (g.M > (1ll << 31) / 2 || g.N > (1ll << 31) / 2 || g.K > (1ll << 31) / 2) {
+    if (err) *err = "run_gemm: dimension too large";
+    return -2;
+  }
+  int* status = device_status_ptr(err);
+  if (!status) return -3;
+  KParams kp{};
+  kp.M = static_cast<int>(g.M);
+  kp.N = static_cast<int>(g.N);
+  kp.K = static_cast<int>(g.K);
+  kp.A = g.A;
+  kp.lda = g.lda;
+  kp.B = g.B;
+  kp.ldb = g.ldb;
+  kp.C = g.C;
+  kp.ldc = g.ldc;
+  kp.gamma = g.gamma;
+  kp.eps = g.eps;
+  kp.bias = g.bias;
+  kp.gelu = g.gelu;
+  kp.residual = g.residual;
+  kp.ldr = g.ldr;
+  kp.vec_ok = (g.ldc % 8 == 0) && aligned16(g.C) && (!g.residual || (g.ldr % 8 == 0 && aligned16(g.residual))) &&
+              (!g.bias || aligned16(g.bias));
+  kp.status = status;
+  kp.timeout_ns = wait_limit_ns();
+
+  // TMA needs 16-byte aligned bases and row strides; the RMSNorm prologue reads
+  // gamma in 16-byte chunks.
+  const bool tma_ok = aligned16(g.A) && aligned16(g.B) && (g.lda % 8 == 0) && (g.ldb % 8 == 0) &&
+                      (!g.gamma || (aligned16(g.gamma) && g.K % 8 == 0));
+  const bool rms = g.gamma != nullptr;
+  if (rms && !tma_ok && (g.K % 8 != 0 || !aligned16(g.gamma))) {
+    if (err) *err = "fused RMSNorm path needs K % 8 == 0 and a 16-byte aligned gamma";
+    return -2;
+  }
+  const int num_tiles = static_cast<int>(((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN));
+  const int grid = num_tiles < sm_count() ? num_tiles : sm_count();
+
+  CUtensorMap ta{}, tb{};
+  if (tma_ok) {
+    if (!make_map(&ta, g.A, g.M, g.K, g.lda, BM, err)) return -3;
+    if (!make_map(&tb, g.B, g.K, g.N, g.ldb, BK, err)) return -3;
+    return rms ? launch<true, false>(kp, ta, tb, grid, stream, err)
+               : launch<false, false>(kp, ta, tb, grid, stream, err);
+  }
+  return rms ? launch<true, true>(kp, ta, tb, grid, stream, err) : launch<false, true>(kp, ta, tb, grid, stream, err);
+}
+
+}  // namespace tfb200
