@@ -114,8 +114,18 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, SmemCtl
   return ok;
 }
 
+// Warps that run the RMSNorm prologue: 8 (two threads per row) with TMA loads,
+// 4 (one thread per row) when the plain-load producer also needs warps.
 template <bool RMS, bool MANUAL>
-__global__ void __launch_bounds__(256 + (RMS ? 128 : 0) + (MANUAL ? 128 : 0), 1)
+struct Roles {
+  static constexpr int kXformWarps = RMS ? (MANUAL ? 4 : 8) : 0;
+  static constexpr int kXformWarp0 = 8;
+  static constexpr int kLoadWarp0 = 8 + kXformWarps;
+  static constexpr int kThreads = 256 + kXformWarps * 32 + (MANUAL ? 128 : 0);
+};
+
+template <bool RMS, bool MANUAL>
+__global__ void __launch_bounds__(Roles<RMS, MANUAL>::kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const KParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -126,19 +136,21 @@ __global__ void __launch_bounds__(256 + (RMS ? 128 : 0) + (MANUAL ? 128 : 0), 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  constexpr int kXformWarp0 = 8;
-  constexpr int kLoadWarp0 = RMS ? 12 : 8;
+  using R = Roles<RMS, MANUAL>;
+  constexpr int kXformWarp0 = R::kXformWarp0;
+  constexpr int kLoadWarp0 = R::kLoadWarp0;
+  constexpr int kXformThreads = R::kXformWarps * 32;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(&ctl->full[s]), MANUAL ? 128 : 1);
       mbar_init(smem_u32(&ctl->empty[s]), 1);
-      mbar_init(smem_u32(&ctl->xfull[s]), 128);
+      mbar_init(smem_u32(&ctl->xfull[s]), kXformThreads > 0 ? kXformThreads : 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&ctl->tfull[b]), 1);
       mbar_init(smem_u32(&ctl->tempty[b]), 128);
-      mbar_init(smem_u32(&ctl->ifull[b]), 128);
+      mbar_init(smem_u32(&ctl->ifull[b]), kXformThreads > 0 ? kXformThreads : 1);
     }
     mbar_init(smem_u32(&ctl->drain), 1);
     ctl->abort = 0;
@@ -341,9 +353,16 @@ __global__ void __launch_bounds__(256 + (RMS ? 128 : 0) + (MANUAL ? 128 : 0), 1)
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl->tempty[acc]));
     }
-  } else if (RMS && warp >= kXformWarp0 && warp < kXformWarp0 + 4) {
+  } else if (RMS && warp >= kXformWarp0 && warp < kXformWarp0 + R::kXformWarps) {
     // -------------------------------------------------------- RMSNorm prologue
-    const int r = threadIdx.x - kXformWarp0 * 32;  // row within the tile
+    // TPR threads share a row; thread h of a row takes 16-byte chunks
+    // h*CPT .. h*CPT+CPT-1 of each 64-column stage (lane pairs then hit 8
+    // distinct bank groups per quarter-warp under the 128-byte swizzle).
+    constexpr int TPR = kXformThreads >= BM ? kXformThreads / BM : 1;
+    constexpr int CPT = 8 / TPR;
+    const int tid = threadIdx.x - kXformWarp0 * 32;
+    const int r = tid / TPR;
+    const int h = tid % TPR;
     int stage = 0;
     uint32_t phase = 0;
     int i = 0;
@@ -351,7 +370,7 @@ __global__ void __launch_bounds__(256 + (RMS ? 128 : 0) + (MANUAL ? 128 : 0), 1)
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++i) {
       const int acc = i & 1;
       const uint32_t use = static_cast<uint32_t>(i >> 1);
-      float ss = 0.0f;
+      uint64_t ss2 = 0;  // two fp32 partial sums (even / odd columns)
       for (int kb = 0; kb < kblocks; ++kb) {
         if (!warp_wait(smem_u32(&ctl->full[stage]), phase, ctl, p)) {
           ok = false;
@@ -359,32 +378,30 @@ __global__ void __launch_bounds__(256 + (RMS ? 128 : 0) + (MANUAL ? 128 : 0), 1)
         }
         uint8_t* rowp = sA + stage * A_STAGE_BYTES + r * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int cc = 0; cc < CPT; ++cc) {
+          const int c = h * CPT + cc;
           const int k0 = kb * BK + c * 8;
           uint4* cp = reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4));
           const uint4 xv = *cp;
           uint4 gv = make_uint4(0u, 0u, 0u, 0u);
           if (k0 < p.K) gv = __ldg(reinterpret_cast<const uint4*>(p.gamma + k0));
-          const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-          uint32_t ow[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float x0 = bf16_lo(xw[e]), x1 = bf16_hi(xw[e]);
-            ss = fmaf(x0, x0, ss);
-            ss = fmaf(x1, x1, ss);
-            ow[e] = pack_bf16(x0 * bf16_lo(gw[e]), x1 * bf16_hi(gw[e]));
-          }
-          *cp = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+          ss2 = sq_acc_bf16x2(ss2, xv.x);
+          ss2 = sq_acc_bf16x2(ss2, xv.y);
+          ss2 = sq_acc_bf16x2(ss2, xv.z);
+          ss2 = sq_acc_bf16x2(ss2, xv.w);
+          *cp = make_uint4(mul_bf16x2(xv.x, gv.x), mul_bf16x2(xv.y, gv.y), mul_bf16x2(xv.z, gv.z),
+                           mul_bf16x2(xv.w, gv.w));
         }
         fence_proxy_async_smem();
         if (kb == kblocks - 1) {
+          float ss = __uint_as_float(static_cast<uint32_t>(ss2)) + __uint_as_float(static_cast<uint32_t>(ss2 >> 32));
+          if (TPR == 2) ss += __shfl_xor_sync(0xffffffffu, ss, 1);
           // The epilogue of the tile that last used this slot must be done with it.
           if (!warp_wait(smem_u32(&ctl->tempty[acc]), (use & 1u) ^ 1u, ctl, p)) {
             ok = false;
             break;
           }
-          ctl->inv[acc][r] = 1.0f / sqrtf(ss / static_cast<float>(p.K) + p.eps);
+          if (h == 0) ctl->inv[acc][r] = 1.0f / sqrtf(ss / static_cast<float>(p.K) + p.eps);
           mbar_arrive(smem_u32(&ctl->ifull[acc]));
         }
         mbar_arrive(smem_u32(&ctl->xfull[stage]));
@@ -513,8 +530,7 @@ int launch(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int 
     }
     attr_set[dev] = true;
   }
-  constexpr int threads = 256 + (RMS ? 128 : 0) + (MANUAL ? 128 : 0);
-  kern<<<grid, threads, smem, s>>>(ta, tb, kp);
+  kern<<<grid, Roles<RMS, MANUAL>::kThreads, smem, s>>>(ta, tb, kp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     if (err) *err = std::string("gemm launch: ") + cudaGetErrorString(e);

@@ -182,4 +182,19 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// bf16x2 product rounded once to nearest even: bit-identical to rounding the
+// exact fp32 product of two bf16 values.
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// acc (two packed fp32 sums) += (lo(x)^2, hi(x)^2) for a bf16x2 word x.
+__device__ __forceinline__ uint64_t sq_acc_bf16x2(uint64_t acc, uint32_t x) {
+  const uint64_t xx = (static_cast<uint64_t>(x & 0xFFFF0000u) << 32) | static_cast<uint64_t>(x << 16);
+  asm("fma.rn.f32x2 %0, %1, %1, %0;" : "+l"(acc) : "l"(xx));
+  return acc;
+}
+
 }  // namespace tfb200

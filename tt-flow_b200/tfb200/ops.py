@@ -18,6 +18,7 @@ ABI; there is no other code path. Shape errors raise ``ValueError`` (numpy's
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -38,7 +39,7 @@ def _rows2d(t: torch.Tensor, name: str) -> torch.Tensor:
         raise TypeError(f"{name} must be bfloat16 (got {t.dtype})")
     if t.dim() < 2:
         raise ValueError(f"{name} must have at least 2 dimensions")
-    t2 = t.reshape(-1, t.shape[-1])
+    t2 = t.reshape(math.prod(t.shape[:-1]), t.shape[-1])
     if t2.stride(-1) != 1:
         t2 = t2.contiguous()
     return t2
