@@ -15,8 +15,9 @@
  *  - Matrices are row-major bf16 in device memory, described by tfb200_mat
  *    (ld = leading dimension in elements, >= cols). Vectors (gamma, b1) are
  *    contiguous bf16 device arrays.
- *  - The caller owns every buffer; the library allocates no device memory and
- *    never frees caller memory.
+ *  - The caller owns every buffer; the library calls no device allocator and
+ *    never frees caller memory. The only device memory it holds is static: a
+ *    status word and the fixed scratch of tfb200_fused_mlp_noalloc.
  *  - Calls are asynchronous and ordered on `stream` (a cudaStream_t; NULL is the
  *    legacy default stream). Distinct host threads may call concurrently on
  *    distinct streams.
@@ -103,6 +104,26 @@ size_t tfb200_fused_mlp_workspace_size(int64_t m, int64_t k, int64_t h, int64_t 
 int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w1, const void* b1,
                      const tfb200_mat* w2, const tfb200_mat* residual, float eps, int gelu_mode, tfb200_mat* y,
                      void* stream, void* workspace, size_t workspace_bytes);
+
+/* Size of the fixed device scratch behind tfb200_fused_mlp_noalloc (8 MiB). */
+#define TFB200_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
+
+/* tfb200_fused_mlp for callers that cannot allocate device memory -- plugin
+ * hosts and inference servers that own every byte of the GPU's memory, or
+ * latency-critical loops that must not risk the synchronisation of an
+ * allocation. Same arguments and result as tfb200_fused_mlp, minus the
+ * workspace: the hidden block (rows x hidden bf16, rounded up to 256 bytes)
+ * lives in a fixed TFB200_NOALLOC_SCRATCH_BYTES device array that the library
+ * holds on every GPU that loads it, until the process exits. Larger problems are
+ * refused with TFB200_EINVAL and a message, before any launch. The first call on
+ * a device looks up the array's device address (cudaGetSymbolAddress); make that
+ * first call before any stream capture. All calls on a device share the array:
+ * calls whose kernels may overlap on the GPU race on it and must be ordered by
+ * the caller. Allocates nothing and calls no allocating routine.
+ * This entry point has no counterpart in the reference. */
+int tfb200_fused_mlp_noalloc(const tfb200_mat* x, const void* gamma, const tfb200_mat* w1, const void* b1,
+                             const tfb200_mat* w2, const tfb200_mat* residual, float eps, int gelu_mode,
+                             tfb200_mat* y, void* stream);
 
 /* Device status word of the current device: TFB200_OK, or TFB200_ETIMEOUT if a
  * kernel's bounded wait ran out since the last clear. Synchronises the device. */

@@ -96,6 +96,8 @@ int sm_count() {
   return counts[dev];
 }
 
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+
 uint64_t launches() { return g_launches.load(); }
 void count_launch(uint64_t n) { g_launches.fetch_add(n); }
 uint64_t wait_limit_ns() { return g_wait_ns.load(); }

@@ -42,6 +42,9 @@ int run_gemm(const GemmProblem& p, cudaStream_t stream, std::string* err);
 // Device status word (per device): set by kernels whose bounded waits ran out.
 int* device_status_ptr(std::string* err);
 
+// Set the message tfb200_last_error() returns on this thread.
+void set_last_error(const std::string& msg);
+
 // SM count of the current device (cached).
 int sm_count();
 

@@ -25,6 +25,7 @@ TFB200_BF16 = 0
 TFB200_F32 = 1
 TFB200_GELU_ERF = 0
 TFB200_GELU_TANH = 1
+TFB200_NOALLOC_SCRATCH_BYTES = 8 * 1024 * 1024
 
 # Every symbol include/tfb200.h declares (checked by tests/test_abi.py).
 EXPORTS = (
@@ -34,6 +35,7 @@ EXPORTS = (
     "tfb200_fused_rmsnorm_matmul",
     "tfb200_fused_mlp_workspace_size",
     "tfb200_fused_mlp",
+    "tfb200_fused_mlp_noalloc",
     "tfb200_device_status",
     "tfb200_clear_device_status",
     "tfb200_set_wait_limit_ns",
@@ -76,6 +78,7 @@ def lib() -> ctypes.CDLL:
         "tfb200_fused_rmsnorm_matmul": ([P, vp, P, f32, P, vp], i32),
         "tfb200_fused_mlp_workspace_size": ([ctypes.c_int64] * 4, sz),
         "tfb200_fused_mlp": ([P, vp, P, vp, P, P, f32, i32, P, vp, vp, sz], i32),
+        "tfb200_fused_mlp_noalloc": ([P, vp, P, vp, P, P, f32, i32, P, vp], i32),
         "tfb200_device_status": ([], i32),
         "tfb200_clear_device_status": ([], i32),
         "tfb200_set_wait_limit_ns": ([u64], None),
