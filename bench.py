@@ -237,9 +237,10 @@ def run_ours(args) -> int:
     elif wl.kind == "fused_rmsnorm_matmul":
         x, g, w = (dev(t[k]) for k in ("x", "gamma", "w"))
         y = torch.empty(d["M"], d["N"], dtype=torch.bfloat16, device="cuda")
+        ws = torch.empty(ops.rmsnorm_matmul_workspace_bytes(d["M"], d["K"], d["N"]), dtype=torch.uint8, device="cuda")
 
         def step(xin=None):
-            ops.fused_rmsnorm_matmul(x if xin is None else xin, g, w, wl.eps, out=y)
+            ops.fused_rmsnorm_matmul(x if xin is None else xin, g, w, wl.eps, out=y, workspace=ws)
         in_bytes = x.numel() * 2
     else:
         x, b = dev(t["a"]), dev(t["b"])

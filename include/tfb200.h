@@ -76,19 +76,26 @@ const char* tfb200_last_error(void);
  * K == 0 writes zeros; M == 0 or N == 0 is a no-op. */
 int tfb200_matmul(const tfb200_mat* a, const tfb200_mat* b, tfb200_mat* c, void* stream);
 
+/* Bytes of device workspace tfb200_fused_rmsnorm_matmul needs for M rows of
+ * width K (the staged bf16(x * gamma) block and the per-row inverse RMS). */
+size_t tfb200_fused_rmsnorm_matmul_workspace_size(int64_t m, int64_t k, int64_t n);
+
 /* Y = rmsnorm(X, gamma, eps) @ W with rmsnorm(x) = x / sqrt(mean_k(x^2) + eps) * gamma.
- * X [M,K], gamma [K], W [K,N], Y [M,N]; K % 8 == 0. The inverse RMS is computed
- * inside the GEMM from the staged activation tiles and applied to the fp32
- * accumulator; the MMA consumes bf16(x * gamma).
+ * X [M,K], gamma [K], W [K,N], Y [M,N]. One HBM-bound pass stages
+ * bf16(x * gamma) and 1/rms per row in `workspace` (>=
+ * tfb200_fused_rmsnorm_matmul_workspace_size bytes, 256-byte aligned); the
+ * tcgen05 GEMM consumes the staged block and scales each fp32 accumulator row
+ * by 1/rms in its epilogue.
  * Replaces the fused RMSNorm+MatMul compute kernel (EmitCompute.cpp:60-255) and
  * host program (EmitHost.cpp:581-978); semantics of golden.fused_rmsnorm_matmul
  * (golden.py:97-102) and of the dialect op tensixflow.fused_rmsnorm_matmul
  * (TensixflowOps.td:230-253; verifier TensixflowOps.cpp:197-278). */
 int tfb200_fused_rmsnorm_matmul(const tfb200_mat* x, const void* gamma, const tfb200_mat* w, float eps,
-                                tfb200_mat* y, void* stream);
+                                tfb200_mat* y, void* stream, void* workspace, size_t workspace_bytes);
 
 /* Bytes of device workspace tfb200_fused_mlp needs for M rows, K model width,
- * H hidden width and N output width (the bf16 hidden activation block). */
+ * H hidden width and N output width (the bf16 hidden activation block plus the
+ * RMSNorm staging of tfb200_fused_rmsnorm_matmul_workspace_size). */
 size_t tfb200_fused_mlp_workspace_size(int64_t m, int64_t k, int64_t h, int64_t n);
 
 /* Y = gelu(rmsnorm(X, gamma, eps) @ W1 + b1) @ W2 + R.
@@ -96,7 +103,7 @@ size_t tfb200_fused_mlp_workspace_size(int64_t m, int64_t k, int64_t h, int64_t 
  * R [M,N] (residual; may alias X when N == K), Y [M,N]. gelu_mode is
  * TFB200_GELU_ERF (the reference's exact form) or TFB200_GELU_TANH.
  * The hidden block is kept as bf16 in `workspace` (>= tfb200_fused_mlp_workspace_size
- * bytes, 256-byte aligned).
+ * bytes, 256-byte aligned), next to the RMSNorm staging.
  * Replaces the fused MLP compute kernel (EmitCompute.cpp:331-558) and host
  * program (EmitHost.cpp:980-1502); semantics of golden.fused_mlp
  * (golden.py:105-122) and of tensixflow.fused_mlp (TensixflowOps.td:259-285;
@@ -112,8 +119,9 @@ int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w
  * hosts and inference servers that own every byte of the GPU's memory, or
  * latency-critical loops that must not risk the synchronisation of an
  * allocation. Same arguments and result as tfb200_fused_mlp, minus the
- * workspace: the hidden block (rows x hidden bf16, rounded up to 256 bytes)
- * lives in a fixed TFB200_NOALLOC_SCRATCH_BYTES device array that the library
+ * workspace: the workspace tfb200_fused_mlp_workspace_size reports (the hidden
+ * block and the RMSNorm staging) lives in a fixed TFB200_NOALLOC_SCRATCH_BYTES
+ * device array that the library
  * holds on every GPU that loads it, until the process exits. Larger problems are
  * refused with TFB200_EINVAL and a message, before any launch. The first call on
  * a device looks up the array's device address (cudaGetSymbolAddress); make that

@@ -45,9 +45,13 @@ def test_library_exports_every_declared_symbol(L):
 def test_version_and_workspace(L):
     lib = L.lib()
     assert lib.tfb200_version() == 1
-    assert lib.tfb200_fused_mlp_workspace_size(8192, 4096, 16384, 4096) == 8192 * 16384 * 2
+    # hidden block + staged bf16(x * gamma) + per-row inverse RMS, each 256-byte aligned
+    assert lib.tfb200_fused_mlp_workspace_size(8192, 4096, 16384, 4096) == 8192 * 16384 * 2 + 8192 * 4096 * 2 + 8192 * 4
     assert lib.tfb200_fused_mlp_workspace_size(0, 4096, 16384, 4096) == 0
-    assert lib.tfb200_fused_mlp_workspace_size(3, 8, 5, 8) == 256
+    assert lib.tfb200_fused_mlp_workspace_size(3, 8, 5, 8) == 3 * 256
+    assert lib.tfb200_fused_rmsnorm_matmul_workspace_size(8192, 4096, 6144) == 8192 * 4096 * 2 + 8192 * 4
+    # the staged block's leading dimension is rounded up to 8 elements for TMA
+    assert lib.tfb200_fused_rmsnorm_matmul_workspace_size(100, 50, 7) == 11264 + 512  # 100*56*2 -> 11264
 
 
 def test_host_validation_needs_no_device(L):

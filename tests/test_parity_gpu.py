@@ -81,7 +81,7 @@ def test_mlp_block_small(ops, golden_vectors, gelu):
     assert_parity(y, g, f"mlp_block_small/{gelu}")
 
 
-RAGGED = [(1, 64, 8), (200, 136, 300), (129, 64, 257), (300, 520, 40), (64, 4096, 1000)]
+RAGGED = [(1, 64, 8), (200, 136, 300), (129, 64, 257), (300, 520, 40), (64, 4096, 1000), (70, 60, 33), (5, 7, 3)]
 
 
 @pytest.mark.parametrize("m,k,n", RAGGED)
@@ -148,10 +148,20 @@ def test_errors_are_loud(ops):
                                  torch.ones(64, 8, dtype=torch.bfloat16, device="cuda"))
     with pytest.raises(TypeError):
         ops.matmul(x.float(), torch.ones(64, 8, device="cuda"))
-    x5 = torch.ones(4, 60, dtype=torch.bfloat16, device="cuda")
-    with pytest.raises(TFB200Error):  # K % 8 != 0 is refused by the fused path
-        ops.fused_rmsnorm_matmul(x5, torch.ones(60, dtype=torch.bfloat16, device="cuda"),
-                                 torch.ones(60, 8, dtype=torch.bfloat16, device="cuda"))
+    import ctypes
+
+    from tfb200 import _lib as L
+
+    w = torch.ones(64, 8, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(4, 8, dtype=torch.bfloat16, device="cuda")
+    tiny = torch.empty(256, dtype=torch.uint8, device="cuda")
+    rc = L.lib().tfb200_fused_rmsnorm_matmul(ctypes.byref(ops.mat(x)), ctypes.c_void_p(g.data_ptr()),
+                                             ctypes.byref(ops.mat(w)), ctypes.c_float(1e-5), ctypes.byref(ops.mat(y)),
+                                             ctypes.c_void_p(ops.stream_ptr()), ctypes.c_void_p(tiny.data_ptr()),
+                                             ctypes.c_size_t(256))
+    assert rc == L.TFB200_EWORKSPACE and b"workspace" in L.lib().tfb200_last_error()
+    with pytest.raises(TFB200Error):
+        L.check(rc)
 
 
 # ------------------------------------------------------------ full-size workloads

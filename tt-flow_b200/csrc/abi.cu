@@ -168,8 +168,14 @@ int tfb200_matmul(const tfb200_mat* a, const tfb200_mat* b, tfb200_mat* c, void*
   return rc ? fail(rc, "tfb200_matmul: " + err) : TFB200_OK;
 }
 
+size_t tfb200_fused_rmsnorm_matmul_workspace_size(int64_t m, int64_t k, int64_t n) {
+  (void)n;
+  if (m <= 0 || k <= 0) return 0;
+  return rms_prep_bytes(m, k);
+}
+
 int tfb200_fused_rmsnorm_matmul(const tfb200_mat* x, const void* gamma, const tfb200_mat* w, float eps,
-                                tfb200_mat* y, void* stream) {
+                                tfb200_mat* y, void* stream, void* workspace, size_t workspace_bytes) {
   std::string err;
   if (!mat_ok(x, "x", &err) || !mat_ok(w, "w", &err) || !mat_ok(y, "y", &err))
     return fail(TFB200_EINVAL, "tfb200_fused_rmsnorm_matmul: " + err);
@@ -179,30 +185,39 @@ int tfb200_fused_rmsnorm_matmul(const tfb200_mat* x, const void* gamma, const tf
   if (y->rows == 0 || y->cols == 0) return TFB200_OK;
   if (x->cols == 0) return fail(TFB200_EINVAL, "tfb200_fused_rmsnorm_matmul: RMSNorm over an empty dimension");
   if (!gamma) return fail(TFB200_EINVAL, "tfb200_fused_rmsnorm_matmul: null gamma");
-  if (x->cols % 8 != 0)
-    return fail(TFB200_EUNSUPPORTED, "tfb200_fused_rmsnorm_matmul: K must be a multiple of 8");
+  const size_t need = tfb200_fused_rmsnorm_matmul_workspace_size(x->rows, x->cols, w->cols);
+  if (!workspace || workspace_bytes < need)
+    return fail(TFB200_EWORKSPACE,
+                "tfb200_fused_rmsnorm_matmul: workspace smaller than tfb200_fused_rmsnorm_matmul_workspace_size()");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+    return fail(TFB200_EWORKSPACE, "tfb200_fused_rmsnorm_matmul: workspace must be 256-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  bf16* a = nullptr;
+  int64_t lda = 0;
+  float* inv = nullptr;
+  int rc = run_rms_prep(as_bf16(x->data), x->ld, as_bf16(gamma), x->rows, x->cols, eps, workspace, &a, &lda, &inv,
+                        s, &err);
+  if (rc) return fail(rc, "tfb200_fused_rmsnorm_matmul: " + err);
   GemmProblem g;
   g.M = x->rows;
   g.N = w->cols;
   g.K = x->cols;
-  g.A = as_bf16(x->data);
-  g.lda = x->ld;
+  g.A = a;
+  g.lda = lda;
   g.B = as_bf16(w->data);
   g.ldb = w->ld;
   g.C = static_cast<bf16*>(y->data);
   g.ldc = y->ld;
-  g.gamma = as_bf16(gamma);
-  g.eps = eps;
-  int rc = run_gemm(g, static_cast<cudaStream_t>(stream), &err);
+  g.row_scale = inv;
+  rc = run_gemm(g, s, &err);
   return rc ? fail(rc, "tfb200_fused_rmsnorm_matmul: " + err) : TFB200_OK;
 }
 
 size_t tfb200_fused_mlp_workspace_size(int64_t m, int64_t k, int64_t h, int64_t n) {
-  (void)k;
   (void)n;
-  if (m <= 0 || h <= 0) return 0;
-  const size_t bytes = static_cast<size_t>(m) * static_cast<size_t>(h) * 2;
-  return (bytes + 255) & ~static_cast<size_t>(255);
+  if (m <= 0 || h <= 0 || k <= 0) return 0;
+  const size_t hid = (static_cast<size_t>(m) * static_cast<size_t>(h) * 2 + 255) & ~static_cast<size_t>(255);
+  return hid + rms_prep_bytes(m, k);
 }
 
 int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w1, const void* b1,
@@ -223,7 +238,6 @@ int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w
   if (M == 0 || N == 0) return TFB200_OK;
   if (K == 0) return fail(TFB200_EINVAL, "tfb200_fused_mlp: RMSNorm over an empty dimension");
   if (!gamma) return fail(TFB200_EINVAL, "tfb200_fused_mlp: null gamma");
-  if (K % 8 != 0) return fail(TFB200_EUNSUPPORTED, "tfb200_fused_mlp: K must be a multiple of 8");
   if (H == 0) return fail(TFB200_EUNSUPPORTED, "tfb200_fused_mlp: empty hidden dimension");
   const size_t need = tfb200_fused_mlp_workspace_size(M, K, H, N);
   if (!workspace || workspace_bytes < need)
@@ -232,21 +246,27 @@ int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w
     return fail(TFB200_EWORKSPACE, "tfb200_fused_mlp: workspace must be 256-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   bf16* hid = static_cast<bf16*>(workspace);
+  const size_t hid_bytes = (static_cast<size_t>(M) * static_cast<size_t>(H) * 2 + 255) & ~static_cast<size_t>(255);
+  bf16* a = nullptr;
+  int64_t lda = 0;
+  float* inv = nullptr;
+  int rc = run_rms_prep(as_bf16(x->data), x->ld, as_bf16(gamma), M, K, eps, static_cast<char*>(workspace) + hid_bytes,
+                        &a, &lda, &inv, s, &err);
+  if (rc) return fail(rc, "tfb200_fused_mlp: " + err);
   GemmProblem g1;
   g1.M = M;
   g1.N = H;
   g1.K = K;
-  g1.A = as_bf16(x->data);
-  g1.lda = x->ld;
+  g1.A = a;
+  g1.lda = lda;
   g1.B = as_bf16(w1->data);
   g1.ldb = w1->ld;
   g1.C = hid;
   g1.ldc = H;
-  g1.gamma = as_bf16(gamma);
-  g1.eps = eps;
+  g1.row_scale = inv;
   g1.bias = as_bf16(b1);
   g1.gelu = gelu_mode == TFB200_GELU_ERF ? kGeluErf : kGeluTanh;
-  int rc = run_gemm(g1, s, &err);
+  rc = run_gemm(g1, s, &err);
   if (rc) return fail(rc, "tfb200_fused_mlp (up projection): " + err);
   GemmProblem g2;
   g2.M = M;

@@ -15,17 +15,17 @@
 //   warp 1      MMA issuer: one thread issues tcgen05.mma 128x256x16 into a
 //               double-buffered fp32 accumulator in TMEM (2 x 256 columns).
 //   warp 2      TMEM allocator.
-//   warps 4-7   epilogue: tcgen05.ld 32 columns at a time, row scale, bias,
-//               GELU, residual, bf16 round, store.
-//   warps 8-11  RMSNorm prologue (only when gamma is given): thread r owns row r
-//               of each A stage, accumulates sum(x^2) in fp32, rewrites the stage
-//               in place as bf16(x * gamma) and hands it to the MMA warp; at the
-//               end of the K loop it publishes 1/sqrt(sum/K + eps) for the
-//               epilogue's row scale. rmsnorm(x) @ W = diag(1/rms) (x*gamma) @ W,
-//               so the activation is read from HBM once.
-//   warps 12-15 (only for operands TMA cannot describe: leading dimensions that
+//   warps 4-7   epilogue: tcgen05.ld 32 columns at a time, row scale (the
+//               RMSNorm inverse RMS), bias, GELU, residual, bf16 round, store.
+//   warps 8-11  (only for operands TMA cannot describe: leading dimensions that
 //               are not multiples of 8 elements or unaligned pointers) plain-load
 //               producer that writes the same swizzled stage layout.
+// For the fused RMSNorm paths A is the bf16(x * gamma) block staged by
+// rmsnorm_prep.cu and the row scale is its 1/rms vector. (An in-mainloop
+// variant that rewrote each TMA-staged A tile in shared memory measured 35%
+// slower at 8192x4096x6144: the hand-off, async-proxy fences, gamma loads and
+// shared-memory traffic all contend with the MMA pipeline, while the staging
+// pass costs one extra HBM round trip of X, 6% of that GEMM.)
 // Every wait is bounded; when one runs out the kernel records kDevTimeout in the
 // device status word, drains what it issued and returns.
 #include <cudaTypedefs.h>
@@ -57,8 +57,7 @@ struct KParams {
   int64_t ldb;
   bf16* C;
   int64_t ldc;
-  const bf16* gamma;
-  float eps;
+  const float* row_scale;
   const bf16* bias;
   int gelu;
   const bf16* residual;
@@ -71,14 +70,11 @@ struct KParams {
 struct SmemCtl {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
-  uint64_t xfull[STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
-  uint64_t ifull[2];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  float inv[2][BM];
 };
 
 constexpr size_t smem_bytes() {
@@ -114,18 +110,14 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, SmemCtl
   return ok;
 }
 
-// Warps that run the RMSNorm prologue: 8 (two threads per row) with TMA loads,
-// 4 (one thread per row) when the plain-load producer also needs warps.
-template <bool RMS, bool MANUAL>
+template <bool MANUAL>
 struct Roles {
-  static constexpr int kXformWarps = RMS ? (MANUAL ? 4 : 8) : 0;
-  static constexpr int kXformWarp0 = 8;
-  static constexpr int kLoadWarp0 = 8 + kXformWarps;
-  static constexpr int kThreads = 256 + kXformWarps * 32 + (MANUAL ? 128 : 0);
+  static constexpr int kLoadWarp0 = 8;
+  static constexpr int kThreads = 256 + (MANUAL ? 128 : 0);
 };
 
-template <bool RMS, bool MANUAL>
-__global__ void __launch_bounds__(Roles<RMS, MANUAL>::kThreads, 1)
+template <bool MANUAL>
+__global__ void __launch_bounds__(Roles<MANUAL>::kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const KParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -136,21 +128,16 @@ __global__ void __launch_bounds__(Roles<RMS, MANUAL>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  using R = Roles<RMS, MANUAL>;
-  constexpr int kXformWarp0 = R::kXformWarp0;
-  constexpr int kLoadWarp0 = R::kLoadWarp0;
-  constexpr int kXformThreads = R::kXformWarps * 32;
+  constexpr int kLoadWarp0 = Roles<MANUAL>::kLoadWarp0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(&ctl->full[s]), MANUAL ? 128 : 1);
       mbar_init(smem_u32(&ctl->empty[s]), 1);
-      mbar_init(smem_u32(&ctl->xfull[s]), kXformThreads > 0 ? kXformThreads : 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&ctl->tfull[b]), 1);
       mbar_init(smem_u32(&ctl->tempty[b]), 128);
-      mbar_init(smem_u32(&ctl->ifull[b]), kXformThreads > 0 ? kXformThreads : 1);
     }
     mbar_init(smem_u32(&ctl->drain), 1);
     ctl->abort = 0;
@@ -233,9 +220,8 @@ __global__ void __launch_bounds__(Roles<RMS, MANUAL>::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < kblocks; ++kb) {
-          const uint32_t wb = RMS ? smem_u32(&ctl->xfull[stage]) : smem_u32(&ctl->full[stage]);
-          if (!mbar_wait(wb, phase, &ctl->abort, p.timeout_ns)) {
+        for (int kb = 0; kb < kblocks && ok; ++kb) {
+          if (!mbar_wait(smem_u32(&ctl->full[stage]), phase, &ctl->abort, p.timeout_ns)) {
             raise_abort(ctl, p.status);
             ok = false;
             break;
@@ -249,6 +235,7 @@ __global__ void __launch_bounds__(Roles<RMS, MANUAL>::kThreads, 1)
             const uint64_t bd = sdesc_sw128(b0 + k * 2048, 8192, 1024);
             mma_bf16(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
+          if (!ok) break;
           mma_commit(smem_u32(&ctl->empty[stage]));
           if (++stage == STAGES) {
             stage = 0;
@@ -274,10 +261,9 @@ __global__ void __launch_bounds__(Roles<RMS, MANUAL>::kThreads, 1)
       const int acc = i & 1;
       const uint32_t use = static_cast<uint32_t>(i >> 1);
       if (!warp_wait(smem_u32(&ctl->tfull[acc]), use & 1u, ctl, p)) break;
-      if (RMS && !warp_wait(smem_u32(&ctl->ifull[acc]), use & 1u, ctl, p)) break;
       tc_fence_after();
       const int64_t row = static_cast<int64_t>(tm) * BM + r;
-      const float scale = RMS ? ctl->inv[acc][r] : 1.0f;
+      const float scale = (p.row_scale && row < p.M) ? __ldg(p.row_scale + row) : 1.0f;
       for (int c = 0; c < BN / 32; ++c) {
         const int col0 = tn * BN + c * 32;
         if (col0 >= p.N) break;  // warp-uniform
@@ -352,64 +338,6 @@ __global__ void __launch_bounds__(Roles<RMS, MANUAL>::kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl->tempty[acc]));
-    }
-  } else if (RMS && warp >= kXformWarp0 && warp < kXformWarp0 + R::kXformWarps) {
-    // -------------------------------------------------------- RMSNorm prologue
-    // TPR threads share a row; thread h of a row takes 16-byte chunks
-    // h*CPT .. h*CPT+CPT-1 of each 64-column stage (lane pairs then hit 8
-    // distinct bank groups per quarter-warp under the 128-byte swizzle).
-    constexpr int TPR = kXformThreads >= BM ? kXformThreads / BM : 1;
-    constexpr int CPT = 8 / TPR;
-    const int tid = threadIdx.x - kXformWarp0 * 32;
-    const int r = tid / TPR;
-    const int h = tid % TPR;
-    int stage = 0;
-    uint32_t phase = 0;
-    int i = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++i) {
-      const int acc = i & 1;
-      const uint32_t use = static_cast<uint32_t>(i >> 1);
-      uint64_t ss2 = 0;  // two fp32 partial sums (even / odd columns)
-      for (int kb = 0; kb < kblocks; ++kb) {
-        if (!warp_wait(smem_u32(&ctl->full[stage]), phase, ctl, p)) {
-          ok = false;
-          break;
-        }
-        uint8_t* rowp = sA + stage * A_STAGE_BYTES + r * 128;
-#pragma unroll
-        for (int cc = 0; cc < CPT; ++cc) {
-          const int c = h * CPT + cc;
-          const int k0 = kb * BK + c * 8;
-          uint4* cp = reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4));
-          const uint4 xv = *cp;
-          uint4 gv = make_uint4(0u, 0u, 0u, 0u);
-          if (k0 < p.K) gv = __ldg(reinterpret_cast<const uint4*>(p.gamma + k0));
-          ss2 = sq_acc_bf16x2(ss2, xv.x);
-          ss2 = sq_acc_bf16x2(ss2, xv.y);
-          ss2 = sq_acc_bf16x2(ss2, xv.z);
-          ss2 = sq_acc_bf16x2(ss2, xv.w);
-          *cp = make_uint4(mul_bf16x2(xv.x, gv.x), mul_bf16x2(xv.y, gv.y), mul_bf16x2(xv.z, gv.z),
-                           mul_bf16x2(xv.w, gv.w));
-        }
-        fence_proxy_async_smem();
-        if (kb == kblocks - 1) {
-          float ss = __uint_as_float(static_cast<uint32_t>(ss2)) + __uint_as_float(static_cast<uint32_t>(ss2 >> 32));
-          if (TPR == 2) ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-          // The epilogue of the tile that last used this slot must be done with it.
-          if (!warp_wait(smem_u32(&ctl->tempty[acc]), (use & 1u) ^ 1u, ctl, p)) {
-            ok = false;
-            break;
-          }
-          if (h == 0) ctl->inv[acc][r] = 1.0f / sqrtf(ss / static_cast<float>(p.K) + p.eps);
-          mbar_arrive(smem_u32(&ctl->ifull[acc]));
-        }
-        mbar_arrive(smem_u32(&ctl->xfull[stage]));
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
     }
   } else if (MANUAL && warp >= kLoadWarp0 && warp < kLoadWarp0 + 4) {
     // ------------------------------------------------- plain-load producer
@@ -514,10 +442,10 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int6
   return true;
 }
 
-template <bool RMS, bool MANUAL>
+template <bool MANUAL>
 int launch(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int grid, cudaStream_t s,
            std::string* err) {
-  auto kern = k_gemm<RMS, MANUAL>;
+  auto kern = k_gemm<MANUAL>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -530,7 +458,7 @@ int launch(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int 
     }
     attr_set[dev] = true;
   }
-  kern<<<grid, Roles<RMS, MANUAL>::kThreads, smem, s>>>(ta, tb, kp);
+  kern<<<grid, Roles<MANUAL>::kThreads, smem, s>>>(ta, tb, kp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     if (err) *err = std::string("gemm launch: ") + cudaGetErrorString(e);
@@ -565,8 +493,7 @@ int run_gemm(const GemmProblem& g, cudaStream_t stream, std::string* err) {
   kp.ldb = g.ldb;
   kp.C = g.C;
   kp.ldc = g.ldc;
-  kp.gamma = g.gamma;
-  kp.eps = g.eps;
+  kp.row_scale = g.row_scale;
   kp.bias = g.bias;
   kp.gelu = g.gelu;
   kp.residual = g.residual;
@@ -576,15 +503,8 @@ int run_gemm(const GemmProblem& g, cudaStream_t stream, std::string* err) {
   kp.status = status;
   kp.timeout_ns = wait_limit_ns();
 
-  // TMA needs 16-byte aligned bases and row strides; the RMSNorm prologue reads
-  // gamma in 16-byte chunks.
-  const bool tma_ok = aligned16(g.A) && aligned16(g.B) && (g.lda % 8 == 0) && (g.ldb % 8 == 0) &&
-                      (!g.gamma || (aligned16(g.gamma) && g.K % 8 == 0));
-  const bool rms = g.gamma != nullptr;
-  if (rms && !tma_ok && (g.K % 8 != 0 || !aligned16(g.gamma))) {
-    if (err) *err = "fused RMSNorm path needs K % 8 == 0 and a 16-byte aligned gamma";
-    return -2;
-  }
+  // TMA needs 16-byte aligned bases and row strides.
+  const bool tma_ok = aligned16(g.A) && aligned16(g.B) && (g.lda % 8 == 0) && (g.ldb % 8 == 0);
   const int num_tiles = static_cast<int>(((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN));
   const int grid = num_tiles < sm_count() ? num_tiles : sm_count();
 
@@ -592,10 +512,9 @@ int run_gemm(const GemmProblem& g, cudaStream_t stream, std::string* err) {
   if (tma_ok) {
     if (!make_map(&ta, g.A, g.M, g.K, g.lda, BM, err)) return -3;
     if (!make_map(&tb, g.B, g.K, g.N, g.ldb, BK, err)) return -3;
-    return rms ? launch<true, false>(kp, ta, tb, grid, stream, err)
-               : launch<false, false>(kp, ta, tb, grid, stream, err);
+    return launch<false>(kp, ta, tb, grid, stream, err);
   }
-  return rms ? launch<true, true>(kp, ta, tb, grid, stream, err) : launch<false, true>(kp, ta, tb, grid, stream, err);
+  return launch<true>(kp, ta, tb, grid, stream, err);
 }
 
 }  // namespace tfb200

@@ -13,11 +13,11 @@ using bf16 = __nv_bfloat16;
 
 enum GeluMode : int { kGeluNone = 0, kGeluErf = 1, kGeluTanh = 2 };
 
-// One GEMM with the fused prologue/epilogue options of this backend:
-//   C[M,N] = epi( rowscale(M) * (prologue(A)[M,K] @ B[K,N]) )
-// prologue(A) = bf16(A * gamma) when gamma != nullptr (RMSNorm: rowscale is then
-// 1/sqrt(mean_k(A^2) + eps), computed from A in the same kernel), else A.
+// One GEMM with the fused epilogue options of this backend:
+//   C[M,N] = epi( row_scale[m] * (A[M,K] @ B[K,N]) )
 // epi(v) = gelu(v + bias[n]) (each part optional), then + residual[m,n].
+// row_scale (fp32, optional) carries the RMSNorm inverse RMS when A is the
+// bf16(x * gamma) block staged by run_rms_prep.
 // All matrices are bf16, row-major, with leading dimensions in elements.
 struct GemmProblem {
   int64_t M = 0, N = 0, K = 0;
@@ -27,8 +27,7 @@ struct GemmProblem {
   int64_t ldb = 0;
   bf16* C = nullptr;
   int64_t ldc = 0;
-  const bf16* gamma = nullptr;
-  float eps = 1e-6f;
+  const float* row_scale = nullptr;
   const bf16* bias = nullptr;
   int gelu = kGeluNone;
   const bf16* residual = nullptr;
@@ -38,6 +37,14 @@ struct GemmProblem {
 // Launch the persistent tcgen05 GEMM. Returns 0 or a negative TFB200_E* code with
 // a message in *err.
 int run_gemm(const GemmProblem& p, cudaStream_t stream, std::string* err);
+
+// RMSNorm staging pass (rmsnorm_prep.cu): writes bf16(x * gamma) with leading
+// dimension staged_ld(K) and inv[m] = 1/sqrt(mean_k(x^2) + eps) into `ws`
+// (rms_prep_bytes(M, K) bytes, 256-byte aligned).
+int64_t staged_ld(int64_t k);
+size_t rms_prep_bytes(int64_t m, int64_t k);
+int run_rms_prep(const bf16* x, int64_t ldx, const bf16* gamma, int64_t M, int64_t K, float eps, void* ws,
+                 bf16** a_out, int64_t* lda_out, float** inv_out, cudaStream_t stream, std::string* err);
 
 // Device status word (per device): set by kernels whose bounded waits ran out.
 int* device_status_ptr(std::string* err);

@@ -14,8 +14,8 @@
 // That first call should therefore come before any stream capture. All calls on
 // a device share the array and it keeps the last call's contents: two calls
 // whose kernels overlap on the GPU (different streams without ordering between
-// them) race on it. Nothing in it has to start at zero: the up-projection
-// writes every hidden element the down-projection then reads.
+// them) race on it. Nothing in it has to start at zero: the staging pass and
+// the up-projection write every element that the later kernels read.
 #include <mutex>
 #include <string>
 
@@ -55,8 +55,8 @@ extern "C" int tfb200_fused_mlp_noalloc(const tfb200_mat* x, const void* gamma, 
   if (x && w1 && w2) {
     const size_t need = tfb200_fused_mlp_workspace_size(x->rows, x->cols, w1->cols, w2->cols);
     if (need > TFB200_NOALLOC_SCRATCH_BYTES) {
-      tfb200::set_last_error("tfb200_fused_mlp_noalloc: the hidden block needs " + std::to_string(need) +
-                             " bytes (rows x hidden x 2, rounded up to 256); the fixed scratch holds " +
+      tfb200::set_last_error("tfb200_fused_mlp_noalloc: the workspace needs " + std::to_string(need) +
+                             " bytes (tfb200_fused_mlp_workspace_size); the fixed scratch holds " +
                              std::to_string(static_cast<size_t>(TFB200_NOALLOC_SCRATCH_BYTES)) +
                              ". Use tfb200_fused_mlp with a workspace, or fewer rows per call.");
       return TFB200_EINVAL;

@@ -1,0 +1,117 @@
+// RMSNorm staging pass of the fused RMSNorm+MatMul and fused MLP paths.
+//
+// One warp per row reads the activation row once from HBM, computes
+// sum(x^2) in fp32, and writes
+//   inv[m]   = 1 / sqrt(sum_k x[m,k]^2 / K + eps)            (fp32)
+//   a[m, k]  = bf16(x[m,k] * gamma[k])                       (bf16, one rounding)
+// The GEMM that follows consumes `a` as its A operand and multiplies each
+// accumulator row by inv[m] in its epilogue, using
+//   rmsnorm(x) @ W = diag(inv) * ((x * gamma) @ W).
+// This replaces the RMSNorm part of the Tensix fused compute kernels
+// (tensixflow lib/tensixflow/Codegen/EmitCompute.cpp:172-213 square / reduce /
+// rsqrt / scale, :437-492 in the MLP kernel). `a` is written with a leading
+// dimension that is a multiple of 8 elements so that TMA can always describe it,
+// whatever the alignment of x.
+//
+// The pass is HBM-bound: 2*M*K bytes read, 2*M*K + 4*M written. The second read
+// of each row (to apply gamma after the sum is known) hits L1/L2.
+#include "internal.h"
+#include "sm100_ptx.cuh"
+
+namespace tfb200 {
+
+namespace {
+
+constexpr int kWarps = 8;
+
+template <bool VEC>
+__global__ void __launch_bounds__(kWarps * 32) k_rms_prep(const bf16* __restrict__ x, int64_t ldx,
+                                                          const bf16* __restrict__ gamma, int M, int K, float eps,
+                                                          bf16* __restrict__ a, int64_t lda,
+                                                          float* __restrict__ inv) {
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5); row < M; row += stride) {
+    const bf16* xr = x + row * ldx;
+    bf16* ar = a + row * lda;
+    float ss = 0.0f;
+    if (VEC) {
+      const uint4* xv = reinterpret_cast<const uint4*>(xr);
+      const int nchunk = K / 8;
+      uint64_t ss2 = 0;
+#pragma unroll 4
+      for (int c = lane; c < nchunk; c += 32) {
+        const uint4 v = __ldg(xv + c);
+        ss2 = sq_acc_bf16x2(ss2, v.x);
+        ss2 = sq_acc_bf16x2(ss2, v.y);
+        ss2 = sq_acc_bf16x2(ss2, v.z);
+        ss2 = sq_acc_bf16x2(ss2, v.w);
+      }
+      ss = __uint_as_float(static_cast<uint32_t>(ss2)) + __uint_as_float(static_cast<uint32_t>(ss2 >> 32));
+    } else {
+      for (int k = lane; k < K; k += 32) {
+        const float v = __bfloat162float(xr[k]);
+        ss = fmaf(v, v, ss);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) inv[row] = 1.0f / sqrtf(ss / static_cast<float>(K) + eps);
+    if (VEC) {
+      const uint4* xv = reinterpret_cast<const uint4*>(xr);
+      const uint4* gv = reinterpret_cast<const uint4*>(gamma);
+      uint4* av = reinterpret_cast<uint4*>(ar);
+      const int nchunk = K / 8;
+#pragma unroll 4
+      for (int c = lane; c < nchunk; c += 32) {
+        const uint4 v = __ldg(xv + c);
+        const uint4 g = __ldg(gv + c);
+        av[c] = make_uint4(mul_bf16x2(v.x, g.x), mul_bf16x2(v.y, g.y), mul_bf16x2(v.z, g.z), mul_bf16x2(v.w, g.w));
+      }
+    } else {
+      for (int k = lane; k < K; k += 32)
+        ar[k] = __float2bfloat16_rn(__bfloat162float(xr[k]) * __bfloat162float(gamma[k]));
+    }
+  }
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int64_t staged_ld(int64_t k) { return (k + 7) / 8 * 8; }
+
+size_t rms_prep_bytes(int64_t m, int64_t k) {
+  const size_t a = static_cast<size_t>(m) * static_cast<size_t>(staged_ld(k)) * 2;
+  const size_t i = static_cast<size_t>(m) * 4;
+  return ((a + 255) & ~size_t(255)) + ((i + 255) & ~size_t(255));
+}
+
+int run_rms_prep(const bf16* x, int64_t ldx, const bf16* gamma, int64_t M, int64_t K, float eps, void* ws,
+                 bf16** a_out, int64_t* lda_out, float** inv_out, cudaStream_t stream, std::string* err) {
+  const int64_t lda = staged_ld(K);
+  bf16* a = static_cast<bf16*>(ws);
+  const size_t abytes = (static_cast<size_t>(M) * lda * 2 + 255) & ~size_t(255);
+  float* inv = reinterpret_cast<float*>(static_cast<char*>(ws) + abytes);
+  const bool vec = K % 8 == 0 && ldx % 8 == 0 && al16(x) && al16(gamma) && al16(a);
+  const int64_t blocks64 = (M + kWarps - 1) / kWarps;
+  const int blocks = static_cast<int>(blocks64 < 65535 * 8 ? blocks64 : 65535 * 8);
+  if (vec)
+    k_rms_prep<true><<<blocks, kWarps * 32, 0, stream>>>(x, ldx, gamma, static_cast<int>(M), static_cast<int>(K),
+                                                         eps, a, lda, inv);
+  else
+    k_rms_prep<false><<<blocks, kWarps * 32, 0, stream>>>(x, ldx, gamma, static_cast<int>(M),
+                                                          static_cast<int>(K), eps, a, lda, inv);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    if (err) *err = std::string("rmsnorm staging launch: ") + cudaGetErrorString(e);
+    return -3;
+  }
+  count_launch();
+  *a_out = a;
+  *lda_out = lda;
+  *inv_out = inv;
+  return 0;
+}
+
+}  // namespace tfb200

@@ -32,6 +32,7 @@ EXPORTS = (
     "tfb200_version",
     "tfb200_last_error",
     "tfb200_matmul",
+    "tfb200_fused_rmsnorm_matmul_workspace_size",
     "tfb200_fused_rmsnorm_matmul",
     "tfb200_fused_mlp_workspace_size",
     "tfb200_fused_mlp",
@@ -75,7 +76,8 @@ def lib() -> ctypes.CDLL:
         "tfb200_version": ([], i32),
         "tfb200_last_error": ([], ctypes.c_char_p),
         "tfb200_matmul": ([P, P, P, vp], i32),
-        "tfb200_fused_rmsnorm_matmul": ([P, vp, P, f32, P, vp], i32),
+        "tfb200_fused_rmsnorm_matmul_workspace_size": ([ctypes.c_int64] * 3, sz),
+        "tfb200_fused_rmsnorm_matmul": ([P, vp, P, f32, P, vp, vp, sz], i32),
         "tfb200_fused_mlp_workspace_size": ([ctypes.c_int64] * 4, sz),
         "tfb200_fused_mlp": ([P, vp, P, vp, P, P, f32, i32, P, vp, vp, sz], i32),
         "tfb200_fused_mlp_noalloc": ([P, vp, P, vp, P, P, f32, i32, P, vp], i32),

@@ -24,7 +24,8 @@ import torch
 
 from . import _lib as L
 
-__all__ = ["matmul", "fused_rmsnorm_matmul", "fused_mlp", "mlp_workspace_bytes", "mat", "stream_ptr"]
+__all__ = ["matmul", "fused_rmsnorm_matmul", "fused_mlp", "mlp_workspace_bytes", "rmsnorm_matmul_workspace_bytes",
+           "mat", "stream_ptr"]
 
 
 def stream_ptr(stream: torch.cuda.Stream | None = None) -> int:
@@ -75,8 +76,18 @@ def matmul(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None) ->
     return y.reshape(*a.shape[:-1], b2.shape[1]) if out is None else y
 
 
+def rmsnorm_matmul_workspace_bytes(m: int, k: int, n: int) -> int:
+    return int(L.lib().tfb200_fused_rmsnorm_matmul_workspace_size(m, k, n))
+
+
+def _workspace(need: int, ws: torch.Tensor | None, device) -> torch.Tensor:
+    if ws is not None and ws.numel() * ws.element_size() >= need:
+        return ws
+    return torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+
+
 def fused_rmsnorm_matmul(x: torch.Tensor, gamma: torch.Tensor, w: torch.Tensor, eps: float = 1e-6,
-                         out: torch.Tensor | None = None) -> torch.Tensor:
+                         out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """``matmul(rmsnorm(x, gamma, eps), w)`` (golden.fused_rmsnorm_matmul)."""
     x2 = _rows2d(x, "x")
     w2 = _rows2d(w, "w")
@@ -85,9 +96,11 @@ def fused_rmsnorm_matmul(x: torch.Tensor, gamma: torch.Tensor, w: torch.Tensor, 
         raise ValueError(f"fused_rmsnorm_matmul: x has K={K} but w has {w2.shape[0]} rows")
     g = _vec(gamma, K, "gamma")
     y = out if out is not None else torch.empty(x2.shape[0], w2.shape[1], dtype=torch.bfloat16, device=x.device)
+    ws = _workspace(rmsnorm_matmul_workspace_bytes(x2.shape[0], K, w2.shape[1]), workspace, x.device)
     L.check(L.lib().tfb200_fused_rmsnorm_matmul(ctypes.byref(mat(x2)), ctypes.c_void_p(g.data_ptr()),
                                                 ctypes.byref(mat(w2)), ctypes.c_float(eps), ctypes.byref(mat(y)),
-                                                ctypes.c_void_p(stream_ptr())))
+                                                ctypes.c_void_p(stream_ptr()), ctypes.c_void_p(ws.data_ptr()),
+                                                ctypes.c_size_t(ws.numel() * ws.element_size())))
     return y.reshape(*x.shape[:-1], w2.shape[1]) if out is None else y
 
 
@@ -125,9 +138,7 @@ def fused_mlp(x: torch.Tensor, gamma: torch.Tensor, w1: torch.Tensor, b1: torch.
     if gelu not in _GELU:
         raise ValueError(f"gelu must be 'erf' or 'tanh' (got {gelu!r})")
     y = out if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
-    need = mlp_workspace_bytes(M, K, H, N)
-    if workspace is None or workspace.numel() * workspace.element_size() < need:
-        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=x.device)
+    workspace = _workspace(mlp_workspace_bytes(M, K, H, N), workspace, x.device)
     L.check(L.lib().tfb200_fused_mlp(
         ctypes.byref(mat(x2)), ctypes.c_void_p(g.data_ptr()), ctypes.byref(mat(W1)),
         ctypes.c_void_p(b.data_ptr() if b is not None else None), ctypes.byref(mat(W2)), ctypes.byref(mat(r2)),
