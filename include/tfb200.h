@@ -112,6 +112,27 @@ int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w
                      const tfb200_mat* w2, const tfb200_mat* residual, float eps, int gelu_mode, tfb200_mat* y,
                      void* stream, void* workspace, size_t workspace_bytes);
 
+/* Tensor-parallel fused MLP, one shard per GPU (the decode-shaped case, M <= 64):
+ * partial[M,N] (fp32, leading dimension ld_partial) =
+ *     gelu(rmsnorm(X, gamma, eps) @ W1s + b1s) @ W2s
+ * where W1s [K, H/G] is this GPU's column shard of W1, b1s the matching slice of
+ * b1 and W2s [H/G, N] the matching row shard of W2. Summing `partial` over the G
+ * GPUs (one all-reduce) and calling tfb200_residual_add gives tfb200_fused_mlp's
+ * result. RMSNorm is computed redundantly on every GPU from the full X. The
+ * reference has no multi-device path (its n300 second chip exists only in the
+ * planner's arithmetic); this splits the same op (golden.py:105-122). */
+size_t tfb200_fused_mlp_partial_workspace_size(int64_t m, int64_t k, int64_t h_shard, int64_t n);
+int tfb200_fused_mlp_partial(const tfb200_mat* x, const void* gamma, const tfb200_mat* w1_shard,
+                             const void* b1_shard, const tfb200_mat* w2_shard, float eps, int gelu_mode,
+                             float* partial, int64_t ld_partial, void* stream, void* workspace,
+                             size_t workspace_bytes);
+
+/* y = bf16(partial + residual): the last step of the tensor-parallel MLP, after
+ * the partial sums have been reduced across GPUs (the residual add of
+ * golden.py:122). partial is fp32 with leading dimension ld_partial. */
+int tfb200_residual_add(const float* partial, int64_t ld_partial, const tfb200_mat* residual, tfb200_mat* y,
+                        void* stream);
+
 /* Size of the fixed device scratch behind tfb200_fused_mlp_noalloc (8 MiB). */
 #define TFB200_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
 
@@ -138,6 +159,13 @@ int tfb200_fused_mlp_noalloc(const tfb200_mat* x, const void* gamma, const tfb20
 int tfb200_device_status(void);
 /* Reset the current device's status word to TFB200_OK. */
 int tfb200_clear_device_status(void);
+
+/* Failure-detection self-test: launches one kernel that waits on a device
+ * barrier nothing completes. Its bounded wait gives up after limit_ns (at most
+ * 10 s) and sets the status word to TFB200_ETIMEOUT; the context stays usable.
+ * No counterpart in the reference (its failure handling is host-side exit codes,
+ * scripts/run_generated.sh:17-23). */
+int tfb200_selftest_bounded_wait(uint64_t limit_ns, void* stream);
 
 /* Wall-time limit of every bounded device wait, in nanoseconds (default 2e9). */
 void tfb200_set_wait_limit_ns(uint64_t ns);

@@ -48,7 +48,9 @@ def test_version_and_workspace(L):
     # hidden block + staged bf16(x * gamma) + per-row inverse RMS, each 256-byte aligned
     assert lib.tfb200_fused_mlp_workspace_size(8192, 4096, 16384, 4096) == 8192 * 16384 * 2 + 8192 * 4096 * 2 + 8192 * 4
     assert lib.tfb200_fused_mlp_workspace_size(0, 4096, 16384, 4096) == 0
-    assert lib.tfb200_fused_mlp_workspace_size(3, 8, 5, 8) == 3 * 256
+    # few rows: the streamed path adds fp32 accumulators and column-block counters
+    assert lib.tfb200_fused_mlp_workspace_size(3, 8, 5, 8) == 7 * 256
+    assert lib.tfb200_fused_mlp_partial_workspace_size(3, 8, 5, 8) == 6 * 256
     assert lib.tfb200_fused_rmsnorm_matmul_workspace_size(8192, 4096, 6144) == 8192 * 4096 * 2 + 8192 * 4
     # the staged block's leading dimension is rounded up to 8 elements for TMA
     assert lib.tfb200_fused_rmsnorm_matmul_workspace_size(100, 50, 7) == 11264 + 512  # 100*56*2 -> 11264

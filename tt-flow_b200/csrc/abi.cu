@@ -34,6 +34,20 @@ __global__ void k_fill_zero_bf16(bf16* c, int64_t rows, int64_t cols, int64_t ld
   }
 }
 
+// Waits on an mbarrier that nothing arrives on; the bounded wait gives up after
+// limit_ns and records the timeout in the status word.
+__global__ void k_wait_selftest(int* status, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort;
+  if (threadIdx.x == 0) {
+    abort = 0;
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !mbar_wait(smem_u32(&bar), 0, &abort, limit_ns)) atomicExch(status, kDevTimeout);
+}
+
 bool mat_ok(const tfb200_mat* m, const char* name, std::string* err) {
   if (!m) {
     *err = std::string(name) + ": null descriptor";
@@ -214,10 +228,14 @@ int tfb200_fused_rmsnorm_matmul(const tfb200_mat* x, const void* gamma, const tf
 }
 
 size_t tfb200_fused_mlp_workspace_size(int64_t m, int64_t k, int64_t h, int64_t n) {
-  (void)n;
   if (m <= 0 || h <= 0 || k <= 0) return 0;
   const size_t hid = (static_cast<size_t>(m) * static_cast<size_t>(h) * 2 + 255) & ~static_cast<size_t>(255);
-  return hid + rms_prep_bytes(m, k);
+  size_t need = hid + rms_prep_bytes(m, k);
+  if (m <= kStreamMaxRows && n > 0) {
+    const size_t d = decode_mlp_bytes(m, k, h, n);
+    if (d > need) need = d;
+  }
+  return need;
 }
 
 int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w1, const void* b1,
@@ -245,6 +263,14 @@ int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w
   if (reinterpret_cast<uintptr_t>(workspace) & 255u)
     return fail(TFB200_EWORKSPACE, "tfb200_fused_mlp: workspace must be 256-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (decode_eligible(M, w1->data, w1->ld, w2->data, w2->ld) && H % 8 == 0) {
+    // Few rows: stream the weights through every SM (swap-AB, split K).
+    int rc = run_decode_mlp(as_bf16(x->data), x->ld, as_bf16(gamma), as_bf16(w1->data), w1->ld, as_bf16(b1),
+                            as_bf16(w2->data), w2->ld, as_bf16(residual->data), residual->ld, eps,
+                            gelu_mode == TFB200_GELU_ERF ? kGeluErf : kGeluTanh, static_cast<bf16*>(y->data), y->ld,
+                            nullptr, 0, M, K, H, N, workspace, s, &err);
+    return rc ? fail(rc, "tfb200_fused_mlp (streamed): " + err) : TFB200_OK;
+  }
   bf16* hid = static_cast<bf16*>(workspace);
   const size_t hid_bytes = (static_cast<size_t>(M) * static_cast<size_t>(H) * 2 + 255) & ~static_cast<size_t>(255);
   bf16* a = nullptr;
@@ -282,6 +308,67 @@ int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w
   g2.ldr = residual->ld;
   rc = run_gemm(g2, s, &err);
   if (rc) return fail(rc, "tfb200_fused_mlp (down projection): " + err);
+  return TFB200_OK;
+}
+
+size_t tfb200_fused_mlp_partial_workspace_size(int64_t m, int64_t k, int64_t h, int64_t n) {
+  if (m <= 0 || k <= 0 || h <= 0 || n <= 0) return 0;
+  return decode_core_bytes(m, k, h, n);
+}
+
+int tfb200_fused_mlp_partial(const tfb200_mat* x, const void* gamma, const tfb200_mat* w1, const void* b1,
+                             const tfb200_mat* w2, float eps, int gelu_mode, float* partial, int64_t ld_partial,
+                             void* stream, void* workspace, size_t workspace_bytes) {
+  std::string err;
+  if (!mat_ok(x, "x", &err) || !mat_ok(w1, "w1", &err) || !mat_ok(w2, "w2", &err))
+    return fail(TFB200_EINVAL, "tfb200_fused_mlp_partial: " + err);
+  const int64_t M = x->rows, K = x->cols, H = w1->cols, N = w2->cols;
+  if (w1->rows != K || w2->rows != H)
+    return fail(TFB200_EINVAL, "tfb200_fused_mlp_partial: shapes do not chain (X[M,K], W1[K,H], W2[H,N])");
+  if (gelu_mode != TFB200_GELU_ERF && gelu_mode != TFB200_GELU_TANH)
+    return fail(TFB200_EINVAL, "tfb200_fused_mlp_partial: bad gelu_mode");
+  if (!(eps >= 0.0f)) return fail(TFB200_EINVAL, "tfb200_fused_mlp_partial: eps must be >= 0");
+  if (M == 0 || N == 0) return TFB200_OK;
+  if (!partial || ld_partial < N) return fail(TFB200_EINVAL, "tfb200_fused_mlp_partial: bad partial buffer");
+  if (!gamma || K == 0) return fail(TFB200_EINVAL, "tfb200_fused_mlp_partial: null gamma or empty K");
+  if (!decode_eligible(M, w1->data, w1->ld, w2->data, w2->ld) || H % 8 != 0)
+    return fail(TFB200_EUNSUPPORTED,
+                "tfb200_fused_mlp_partial: needs M <= 64, 16-byte aligned weights with ld % 8 == 0, H % 8 == 0");
+  const size_t need = tfb200_fused_mlp_partial_workspace_size(M, K, H, N);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(TFB200_EWORKSPACE, "tfb200_fused_mlp_partial: workspace missing, small or not 256-byte aligned");
+  const int rc = run_decode_mlp(as_bf16(x->data), x->ld, as_bf16(gamma), as_bf16(w1->data), w1->ld, as_bf16(b1),
+                                as_bf16(w2->data), w2->ld, nullptr, 0, eps,
+                                gelu_mode == TFB200_GELU_ERF ? kGeluErf : kGeluTanh, nullptr, 0, partial, ld_partial,
+                                M, K, H, N, workspace, static_cast<cudaStream_t>(stream), &err);
+  return rc ? fail(rc, "tfb200_fused_mlp_partial: " + err) : TFB200_OK;
+}
+
+int tfb200_residual_add(const float* partial, int64_t ld_partial, const tfb200_mat* residual, tfb200_mat* y,
+                        void* stream) {
+  std::string err;
+  if (!mat_ok(residual, "residual", &err) || !mat_ok(y, "y", &err))
+    return fail(TFB200_EINVAL, "tfb200_residual_add: " + err);
+  if (residual->rows != y->rows || residual->cols != y->cols)
+    return fail(TFB200_EINVAL, "tfb200_residual_add: residual and y shapes differ");
+  if (y->rows == 0 || y->cols == 0) return TFB200_OK;
+  if (!partial || ld_partial < y->cols) return fail(TFB200_EINVAL, "tfb200_residual_add: bad partial buffer");
+  const int rc = launch_residual_add(partial, ld_partial, as_bf16(residual->data), residual->ld,
+                                     static_cast<bf16*>(y->data), y->ld, y->rows, y->cols,
+                                     static_cast<cudaStream_t>(stream), &err);
+  return rc ? fail(rc, "tfb200_residual_add: " + err) : TFB200_OK;
+}
+
+int tfb200_selftest_bounded_wait(uint64_t limit_ns, void* stream) {
+  std::string err;
+  int* st = device_status_ptr(&err);
+  if (!st) return fail(TFB200_ECUDA, err);
+  if (limit_ns == 0 || limit_ns > 10000000000ull)
+    return fail(TFB200_EINVAL, "tfb200_selftest_bounded_wait: limit must be in (0, 10 s]");
+  k_wait_selftest<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(st, limit_ns);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(TFB200_ECUDA, std::string("selftest launch: ") + cudaGetErrorString(e));
+  count_launch();
   return TFB200_OK;
 }
 

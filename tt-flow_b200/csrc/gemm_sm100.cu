@@ -422,6 +422,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn(std::string* err) {
   return fn;
 }
 
+}  // namespace
+
 // Row-major bf16 matrix [rows, cols] with leading dimension ld: box of
 // 64 (cols) x box_rows, 128-byte swizzle, zero fill outside the matrix.
 bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, uint32_t box_rows,
@@ -441,6 +443,8 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int6
   }
   return true;
 }
+
+namespace {
 
 template <bool MANUAL>
 int launch(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int grid, cudaStream_t s,

@@ -1,6 +1,7 @@
 // Host-side interfaces shared by the CUDA translation units of libtfb200.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -37,6 +38,47 @@ struct GemmProblem {
 // Launch the persistent tcgen05 GEMM. Returns 0 or a negative TFB200_E* code with
 // a message in *err.
 int run_gemm(const GemmProblem& p, cudaStream_t stream, std::string* err);
+
+// Weight-streaming GEMM for few rows (stream_sm100.cu): acc[M,N] (+)= A[M,K] @ W[K,N]
+// split over all SMs, then a per-column-block finishing epilogue.
+enum StreamMode : int { kStreamPartial = 0, kStreamFinishUp = 1, kStreamFinishDown = 2 };
+struct StreamProblem {
+  int64_t M = 0, N = 0, K = 0;
+  const bf16* A = nullptr;  // [M, K] tokens
+  int64_t lda = 0;
+  const bf16* W = nullptr;  // [K, N] weights
+  int64_t ldw = 0;
+  float* acc = nullptr;     // [M, N] fp32, zero on entry
+  int* counters = nullptr;  // ceil(N / 128) ints, zero on entry
+  int mode = kStreamPartial;
+  const float* col_scale = nullptr;  // [M] (kStreamFinishUp)
+  const bf16* bias = nullptr;        // [N] (kStreamFinishUp)
+  int gelu = kGeluNone;
+  const bf16* residual = nullptr;    // [M, N] (kStreamFinishDown)
+  int64_t ldr = 0;
+  bf16* out = nullptr;
+  int64_t ldo = 0;
+};
+int run_stream(const StreamProblem& p, cudaStream_t stream, std::string* err);
+int stream_mpad(int64_t m);
+size_t stream_counter_bytes(int64_t n);
+
+// Streamed (decode-shaped) fused MLP, decode.cu. Used for M <= kStreamMaxRows.
+constexpr int64_t kStreamMaxRows = 64;
+size_t decode_core_bytes(int64_t m, int64_t k, int64_t h, int64_t n);
+size_t decode_mlp_bytes(int64_t m, int64_t k, int64_t h, int64_t n);
+bool decode_eligible(int64_t m, const void* w1, int64_t ldw1, const void* w2, int64_t ldw2);
+int run_decode_mlp(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* w1, int64_t ldw1, const bf16* b1,
+                   const bf16* w2, int64_t ldw2, const bf16* residual, int64_t ldr, float eps, int gelu, bf16* y,
+                   int64_t ldy, float* out_partial, int64_t ldp, int64_t M, int64_t K, int64_t H, int64_t N,
+                   void* ws, cudaStream_t s, std::string* err);
+int launch_residual_add(const float* part, int64_t ldp, const bf16* res, int64_t ldr, bf16* y, int64_t ldy,
+                        int64_t M, int64_t N, cudaStream_t s, std::string* err);
+
+// Tensor map of a row-major bf16 matrix [rows, cols] (leading dimension ld),
+// box of 64 columns x box_rows rows, 128-byte swizzle, zero fill outside.
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, uint32_t box_rows,
+              std::string* err);
 
 // RMSNorm staging pass (rmsnorm_prep.cu): writes bf16(x * gamma) with leading
 // dimension staged_ld(K) and inv[m] = 1/sqrt(mean_k(x^2) + eps) into `ws`

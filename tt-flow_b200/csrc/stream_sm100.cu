@@ -1,0 +1,385 @@
+// Weight-streaming (decode-shaped) GEMM for sm_100a: few token rows, large
+// weights. HBM-bound: the job is to stream W at full bandwidth from every SM.
+//
+// Computes acc[M, N] = A[M, K] @ W[K, N] with M <= 256 (tokens) through the
+// transposed product acc^T = W^T A^T ("swap AB"): the MMA's M side is 128 output
+// features (W columns, read N-major straight from row-major W) and its N side is
+// the token count rounded up to 32, so no MMA row is wasted on padding tokens.
+// Work units are (128-column block, 64-deep k block) pairs; the U units are cut
+// into gridDim.x contiguous ranges of equal length (stream-K), so every SM
+// streams the same number of weight bytes whatever the wave count. A CTA
+// accumulates each column block it touches in TMEM, then adds its fp32 partial
+// into `acc` in global memory (L2 atomics). The CTA that completes a column
+// block (a per-block arrival counter) applies the epilogue for that block:
+//   mode kFinishUp:   out = bf16(gelu(acc * col_scale[m] + bias[n]))
+//   mode kFinishDown: out = bf16(acc + residual[m, n])
+//   mode kPartial:    nothing (acc is the result, e.g. a tensor-parallel partial
+//                     sum reduced across GPUs afterwards)
+// `acc` and the counters must be zero on entry (the RMSNorm staging pass clears
+// them).
+//
+// Warp roles: warp 0 TMA producer (W tile 64k x 128n as two 64-column boxes,
+// A tile Mpad x 64k), warp 1 MMA issuer (tcgen05.mma 128 x Mpad x 16, two TMEM
+// accumulators), warp 2 TMEM allocator, warps 4-7 partial-sum and finishing
+// epilogue. All waits are bounded (kDevTimeout in the status word).
+//
+// This is the small-M form of the MLP compute the reference emits
+// (tensixflow lib/tensixflow/Codegen/EmitCompute.cpp:331-558).
+#include <cudaTypedefs.h>
+
+#include "internal.h"
+#include "sm100_ptx.cuh"
+
+namespace tfb200 {
+
+namespace {
+
+constexpr int SBN = 128;  // output features per unit (MMA M)
+constexpr int SBK = 64;   // k per unit
+constexpr uint32_t W_STAGE = SBN * SBK * 2;  // 16 KiB
+constexpr int kMaxStages = 12;
+
+struct SParams {
+  int M, N, K, Mpad;
+  int units, kblocks, nblocks;
+  float* acc;
+  int* counters;
+  int mode;
+  const float* col_scale;
+  const bf16* bias;
+  int gelu;
+  const bf16* residual;
+  int64_t ldr;
+  bf16* out;
+  int64_t ldo;
+  int stages;
+  uint32_t tmem_cols;
+  int* status;
+  uint64_t timeout_ns;
+};
+
+struct SCtl {
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  int finisher;
+};
+
+__device__ __forceinline__ int64_t unit_start(int c, int units, int grid) {
+  return static_cast<int64_t>(c) * units / grid;
+}
+// The CTA whose range holds unit u.
+__device__ __forceinline__ int cta_of(int64_t u, int units, int grid) {
+  return static_cast<int>(((u + 1) * grid + units - 1) / units - 1);
+}
+
+__device__ __forceinline__ void raise_abort(SCtl* ctl, int* status) {
+  ctl->abort = 1;
+  atomicExch(status, kDevTimeout);
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// AND of `ok` over the 128 epilogue threads (named barrier 1): every epilogue
+// warp takes the same branch, so none is left waiting at a later epi_bar().
+__device__ __forceinline__ bool epi_all(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(ok ? 1u : 0u)
+      : "memory");
+  return r != 0;
+}
+
+// Bounded wait by all 128 epilogue threads with a common outcome.
+__device__ __forceinline__ bool epi_wait(uint32_t bar, uint32_t parity, SCtl* ctl, const SParams& p) {
+  const bool ok = epi_all(mbar_wait(bar, parity, &ctl->abort, p.timeout_ns));
+  if (!ok && threadIdx.x == 128) raise_abort(ctl, p.status);
+  return ok;
+}
+
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.0f + tanhf(u));
+}
+
+__global__ void __launch_bounds__(256, 1)
+    k_stream(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA, const SParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const uint32_t a_stage = static_cast<uint32_t>(p.Mpad) * SBK * 2;
+  uint8_t* sW = smem;
+  uint8_t* sA = smem + p.stages * W_STAGE;
+  SCtl* ctl = reinterpret_cast<SCtl*>(sA + p.stages * a_stage);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(smem_u32(&ctl->full[s]), 1);
+      mbar_init(smem_u32(&ctl->empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&ctl->tfull[b]), 1);
+      mbar_init(smem_u32(&ctl->tempty[b]), 128);
+    }
+    mbar_init(smem_u32(&ctl->drain), 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmA);
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), p.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = ctl->tmem_base;
+
+  const int G = gridDim.x;
+  const int64_t u0 = unit_start(blockIdx.x, p.units, G);
+  const int64_t u1 = unit_start(blockIdx.x + 1, p.units, G);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0, armed_phase = 0;
+      bool ok = true;
+      for (int64_t u = u0; u < u1; ++u) {
+        const int nb = static_cast<int>(u / p.kblocks);
+        const int kb = static_cast<int>(u % p.kblocks);
+        if (!mbar_wait(smem_u32(&ctl->empty[stage]), phase ^ 1u, &ctl->abort, p.timeout_ns)) {
+          raise_abort(ctl, p.status);
+          ok = false;
+          break;
+        }
+        const uint32_t fb = smem_u32(&ctl->full[stage]);
+        mbar_arrive_expect_tx(fb, W_STAGE + a_stage);
+        tma_load_2d(smem_u32(sW + stage * W_STAGE), &tmW, fb, nb * SBN, kb * SBK);
+        tma_load_2d(smem_u32(sW + stage * W_STAGE + 8192), &tmW, fb, nb * SBN + 64, kb * SBK);
+        tma_load_2d(smem_u32(sA + stage * a_stage), &tmA, fb, kb * SBK, 0);
+        armed |= 1u << stage;
+        armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+        if (++stage == p.stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < p.stages; ++s)
+          if (armed & (1u << s)) {
+            const uint64_t t0 = global_ns();
+            while (!mbar_test(smem_u32(&ctl->full[s]), (armed_phase >> s) & 1u) &&
+                   global_ns() - t0 < p.timeout_ns) {
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16(SBN, p.Mpad, true, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int seg = 0;
+      int64_t u = u0;
+      while (u < u1 && ok) {
+        const int nb = static_cast<int>(u / p.kblocks);
+        const int64_t seg_end = min(u1, static_cast<int64_t>(nb + 1) * p.kblocks);
+        const int acc = seg & 1;
+        const uint32_t use = static_cast<uint32_t>(seg >> 1);
+        if (!mbar_wait(smem_u32(&ctl->tempty[acc]), (use & 1u) ^ 1u, &ctl->abort, p.timeout_ns)) {
+          raise_abort(ctl, p.status);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * p.Mpad);
+        bool first = true;
+        for (; u < seg_end; ++u) {
+          if (!mbar_wait(smem_u32(&ctl->full[stage]), phase, &ctl->abort, p.timeout_ns)) {
+            raise_abort(ctl, p.status);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t w0 = smem_u32(sW + stage * W_STAGE);
+          const uint32_t a0 = smem_u32(sA + stage * a_stage);
+#pragma unroll
+          for (int k = 0; k < SBK / 16; ++k) {
+            const uint64_t wd = sdesc_sw128(w0 + k * 2048, 8192, 1024);  // MN-major W^T
+            const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);      // K-major tokens
+            mma_bf16(d, wd, ad, idesc, (first && k == 0) ? 0u : 1u);
+          }
+          first = false;
+          mma_commit(smem_u32(&ctl->empty[stage]));
+          if (++stage == p.stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) mma_commit(smem_u32(&ctl->tfull[acc]));
+        ++seg;
+      }
+      mma_commit(smem_u32(&ctl->drain));
+      const uint64_t t0 = global_ns();
+      while (!mbar_test(smem_u32(&ctl->drain), 0) && global_ns() - t0 < p.timeout_ns) {
+      }
+    }
+  } else if (warp >= 4) {
+    const int q = warp & 3;
+    const int et = threadIdx.x - 128;  // 0..127
+    int seg = 0;
+    int64_t u = u0;
+    while (u < u1) {
+      const int nb = static_cast<int>(u / p.kblocks);
+      const int64_t seg_end = min(u1, static_cast<int64_t>(nb + 1) * p.kblocks);
+      u = seg_end;
+      const int acc = seg & 1;
+      const uint32_t use = static_cast<uint32_t>(seg >> 1);
+      ++seg;
+      if (!epi_wait(smem_u32(&ctl->tfull[acc]), use & 1u, ctl, p)) break;
+      tc_fence_after();
+      const int n = nb * SBN + q * 32 + lane;
+      for (int c0 = 0; c0 < p.Mpad; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * p.Mpad + c0),
+                       v);
+        tmem_wait_ld();
+        if (n < p.N) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int m = c0 + j;
+            if (m < p.M) atomicAdd(p.acc + static_cast<int64_t>(m) * p.N + n, __uint_as_float(v[j]));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&ctl->tempty[acc]));
+      if (p.mode == kStreamPartial) continue;
+      // Arrive on the column block's counter; the last contributor finishes it.
+      __threadfence();
+      epi_bar();
+      if (et == 0) {
+        const int64_t first_u = static_cast<int64_t>(nb) * p.kblocks;
+        const int contributors =
+            cta_of(first_u + p.kblocks - 1, p.units, G) - cta_of(first_u, p.units, G) + 1;
+        const int prev = atomicAdd(p.counters + nb, 1);
+        ctl->finisher = (prev == contributors - 1);
+      }
+      epi_bar();
+      if (ctl->finisher) {
+        __threadfence();
+        const int nf = nb * SBN + et;
+        if (nf < p.N) {
+          const float bias = (p.mode == kStreamFinishUp && p.bias) ? __bfloat162float(p.bias[nf]) : 0.0f;
+          for (int m = 0; m < p.M; ++m) {
+            float val = __ldcg(p.acc + static_cast<int64_t>(m) * p.N + nf);
+            if (p.mode == kStreamFinishUp) {
+              val = val * __ldg(p.col_scale + m) + bias;
+              val = p.gelu == kGeluErf ? gelu_erf(val) : (p.gelu == kGeluTanh ? gelu_tanh(val) : val);
+            } else {
+              val += __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ldr + nf]);
+            }
+            p.out[static_cast<int64_t>(m) * p.ldo + nf] = __float2bfloat16_rn(val);
+          }
+        }
+        epi_bar();
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, p.tmem_cols);
+  }
+}
+
+}  // namespace
+
+int stream_mpad(int64_t m) { return static_cast<int>((m + 31) / 32 * 32); }
+
+size_t stream_counter_bytes(int64_t n) { return static_cast<size_t>((n + SBN - 1) / SBN) * sizeof(int); }
+
+int run_stream(const StreamProblem& sp, cudaStream_t stream, std::string* err) {
+  if (sp.M <= 0 || sp.M > 256 || sp.N <= 0 || sp.K <= 0) {
+    if (err) *err = "weight-streaming GEMM: needs 1 <= M <= 256 and N, K > 0";
+    return -2;
+  }
+  if ((reinterpret_cast<uintptr_t>(sp.A) & 15u) || (reinterpret_cast<uintptr_t>(sp.W) & 15u) || sp.lda % 8 ||
+      sp.ldw % 8) {
+    if (err) *err = "weight-streaming GEMM: operands must be 16-byte aligned with leading dimensions % 8 == 0";
+    return -2;
+  }
+  int* status = device_status_ptr(err);
+  if (!status) return -3;
+  SParams p{};
+  p.M = static_cast<int>(sp.M);
+  p.N = static_cast<int>(sp.N);
+  p.K = static_cast<int>(sp.K);
+  p.Mpad = stream_mpad(sp.M);
+  p.kblocks = static_cast<int>((sp.K + SBK - 1) / SBK);
+  p.nblocks = static_cast<int>((sp.N + SBN - 1) / SBN);
+  p.units = p.kblocks * p.nblocks;
+  p.acc = sp.acc;
+  p.counters = sp.counters;
+  p.mode = sp.mode;
+  p.col_scale = sp.col_scale;
+  p.bias = sp.bias;
+  p.gelu = sp.gelu;
+  p.residual = sp.residual;
+  p.ldr = sp.ldr;
+  p.out = sp.out;
+  p.ldo = sp.ldo;
+  p.status = status;
+  p.timeout_ns = wait_limit_ns();
+  const uint32_t a_stage = static_cast<uint32_t>(p.Mpad) * SBK * 2;
+  const size_t budget = 200 * 1024;
+  int stages = static_cast<int>(budget / (W_STAGE + a_stage));
+  p.stages = stages > kMaxStages ? kMaxStages : stages;
+  uint32_t cols = 32;
+  while (cols < static_cast<uint32_t>(2 * p.Mpad)) cols <<= 1;
+  p.tmem_cols = cols;
+  const size_t smem = 1024 + static_cast<size_t>(p.stages) * (W_STAGE + a_stage) + sizeof(SCtl);
+
+  CUtensorMap tw{}, ta{};
+  if (!make_map(&tw, sp.W, sp.K, sp.N, sp.ldw, SBK, err)) return -3;
+  if (!make_map(&ta, sp.A, sp.M, sp.K, sp.lda, static_cast<uint32_t>(p.Mpad), err)) return -3;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) {
+      if (err) *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+      return -3;
+    }
+    attr_set[dev] = true;
+  }
+  const int grid = p.units < sm_count() ? p.units : sm_count();
+  k_stream<<<grid, 256, smem, stream>>>(tw, ta, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    if (err) *err = std::string("weight-streaming GEMM launch: ") + cudaGetErrorString(e);
+    return -3;
+  }
+  count_launch();
+  return 0;
+}
+
+}  // namespace tfb200

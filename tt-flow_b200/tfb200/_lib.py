@@ -37,8 +37,12 @@ EXPORTS = (
     "tfb200_fused_mlp_workspace_size",
     "tfb200_fused_mlp",
     "tfb200_fused_mlp_noalloc",
+    "tfb200_fused_mlp_partial_workspace_size",
+    "tfb200_fused_mlp_partial",
+    "tfb200_residual_add",
     "tfb200_device_status",
     "tfb200_clear_device_status",
+    "tfb200_selftest_bounded_wait",
     "tfb200_set_wait_limit_ns",
     "tfb200_launch_count",
 )
@@ -81,8 +85,12 @@ def lib() -> ctypes.CDLL:
         "tfb200_fused_mlp_workspace_size": ([ctypes.c_int64] * 4, sz),
         "tfb200_fused_mlp": ([P, vp, P, vp, P, P, f32, i32, P, vp, vp, sz], i32),
         "tfb200_fused_mlp_noalloc": ([P, vp, P, vp, P, P, f32, i32, P, vp], i32),
+        "tfb200_fused_mlp_partial_workspace_size": ([ctypes.c_int64] * 4, sz),
+        "tfb200_fused_mlp_partial": ([P, vp, P, vp, P, f32, i32, vp, ctypes.c_int64, vp, vp, sz], i32),
+        "tfb200_residual_add": ([vp, ctypes.c_int64, P, P, vp], i32),
         "tfb200_device_status": ([], i32),
         "tfb200_clear_device_status": ([], i32),
+        "tfb200_selftest_bounded_wait": ([u64, vp], i32),
         "tfb200_set_wait_limit_ns": ([u64], None),
         "tfb200_launch_count": ([], u64),
     }

@@ -24,8 +24,8 @@ import torch
 
 from . import _lib as L
 
-__all__ = ["matmul", "fused_rmsnorm_matmul", "fused_mlp", "mlp_workspace_bytes", "rmsnorm_matmul_workspace_bytes",
-           "mat", "stream_ptr"]
+__all__ = ["matmul", "fused_rmsnorm_matmul", "fused_mlp", "fused_mlp_partial", "residual_add", "mlp_workspace_bytes",
+           "rmsnorm_matmul_workspace_bytes", "mat", "stream_ptr"]
 
 
 def stream_ptr(stream: torch.cuda.Stream | None = None) -> int:
@@ -145,3 +145,40 @@ def fused_mlp(x: torch.Tensor, gamma: torch.Tensor, w1: torch.Tensor, b1: torch.
         ctypes.c_float(eps), ctypes.c_int(_GELU[gelu]), ctypes.byref(mat(y)), ctypes.c_void_p(stream_ptr()),
         ctypes.c_void_p(workspace.data_ptr()), ctypes.c_size_t(workspace.numel() * workspace.element_size())))
     return y.reshape(*x.shape[:-1], N) if out is None else y
+
+
+def fused_mlp_partial(x: torch.Tensor, gamma: torch.Tensor, w1_shard: torch.Tensor, b1_shard: torch.Tensor | None,
+                      w2_shard: torch.Tensor, eps: float = 1e-6, gelu: str = "erf",
+                      out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """One GPU's share of a tensor-parallel MLP: fp32 ``gelu(rmsnorm(x) @ w1_shard + b1_shard) @ w2_shard``
+    (W1 split by columns, W2 by rows). Sum over GPUs, then ``residual_add``."""
+    x2 = _rows2d(x, "x")
+    W1 = _rows2d(w1_shard, "w1_shard")
+    W2 = _rows2d(w2_shard, "w2_shard")
+    M, K = x2.shape
+    H, N = W1.shape[1], W2.shape[1]
+    if W1.shape[0] != K or W2.shape[0] != H:
+        raise ValueError("fused_mlp_partial: shapes do not chain")
+    b = _vec(b1_shard, H, "b1_shard")
+    g = _vec(gamma, K, "gamma")
+    y = out if out is not None else torch.empty(M, N, dtype=torch.float32, device=x.device)
+    ws = _workspace(int(L.lib().tfb200_fused_mlp_partial_workspace_size(M, K, H, N)), workspace, x.device)
+    L.check(L.lib().tfb200_fused_mlp_partial(
+        ctypes.byref(mat(x2)), ctypes.c_void_p(g.data_ptr()), ctypes.byref(mat(W1)),
+        ctypes.c_void_p(b.data_ptr() if b is not None else None), ctypes.byref(mat(W2)), ctypes.c_float(eps),
+        ctypes.c_int(_GELU[gelu]), ctypes.c_void_p(y.data_ptr()), ctypes.c_int64(y.stride(0)),
+        ctypes.c_void_p(stream_ptr()), ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel())))
+    return y
+
+
+def residual_add(partial: torch.Tensor, residual: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``bf16(partial + residual)``: the tail of the tensor-parallel MLP."""
+    if partial.dtype != torch.float32 or partial.dim() != 2 or partial.stride(1) != 1:
+        raise TypeError("partial must be a row-major fp32 matrix")
+    r2 = _rows2d(residual, "residual")
+    if tuple(r2.shape) != tuple(partial.shape):
+        raise ValueError("residual and partial shapes differ")
+    y = out if out is not None else torch.empty(r2.shape, dtype=torch.bfloat16, device=partial.device)
+    L.check(L.lib().tfb200_residual_add(ctypes.c_void_p(partial.data_ptr()), ctypes.c_int64(partial.stride(0)),
+                                        ctypes.byref(mat(r2)), ctypes.byref(mat(y)), ctypes.c_void_p(stream_ptr())))
+    return y
