@@ -383,7 +383,11 @@ def run_ours(args) -> int:
         "clocks": clocks,
     }
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        v, sec, info = cpu_port_tflops(name, args.cpu_rows)
+        rows = args.cpu_rows
+        if rows <= 0:  # size the sample for about 10 s of CPU work
+            _, probe, _ = cpu_port_tflops(name, 64)
+            rows = int(min(d["M"], max(64, 64 * 10.0 / max(probe, 1e-3))))
+        v, sec, info = cpu_port_tflops(name, rows)
         if tp:  # express the CPU rate in the same unit: workload bytes per second
             v = v * 1e12 / flops_step * W.algorithmic_bytes(name) / 1e9
         line["cpu_baseline"] = {"value": v, "unit": unit, "cores": info["cores"], "kind": "port",
@@ -403,7 +407,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="mlp_8192x4096x16384")
-    ap.add_argument("--cpu-rows", type=int, default=1024)
+    ap.add_argument("--cpu-rows", type=int, default=0, help="rows of the CPU baseline sample (0: about 10 s)")
     ap.add_argument("--ref-rows", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -69,19 +69,24 @@ int run_decode_mlp(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* w1
   float* acc2 = out_partial ? out_partial : reinterpret_cast<float*>(base);
   const int64_t ld2 = out_partial ? ldp : N;
 
-  // Accumulators and counters start at zero.
-  cudaError_t e = cudaMemsetAsync(acc1, 0, static_cast<size_t>(static_cast<char*>(static_cast<void*>(cnt2)) -
-                                                               static_cast<char*>(static_cast<void*>(acc1))) +
-                                               stream_counter_bytes(N), s);
-  if (e == cudaSuccess) e = cudaMemset2DAsync(acc2, ld2 * 4, 0, N * 4, M, s);
-  if (e != cudaSuccess) {
-    *err = std::string("decode MLP clear: ") + cudaGetErrorString(e);
-    return -3;
+  // The fp32 accumulators and the column-block counters start at zero: the
+  // staging launch clears the workspace region; a caller's partial buffer with
+  // padding between rows is cleared separately.
+  const size_t clear_bytes = static_cast<size_t>(reinterpret_cast<char*>(cnt2) - reinterpret_cast<char*>(acc1)) +
+                             al256(stream_counter_bytes(N)) +
+                             (out_partial ? 0 : al256(static_cast<size_t>(M) * N * 4));
+  if (out_partial) {
+    const cudaError_t e = ld2 == N ? cudaMemsetAsync(acc2, 0, static_cast<size_t>(M) * N * 4, s)
+                                   : cudaMemset2DAsync(acc2, ld2 * 4, 0, N * 4, M, s);
+    if (e != cudaSuccess) {
+      *err = std::string("decode MLP clear: ") + cudaGetErrorString(e);
+      return -3;
+    }
   }
   bf16* a = nullptr;
   int64_t lda = 0;
   float* inv = nullptr;
-  int rc = run_rms_prep(x, ldx, gamma, M, K, eps, prep, &a, &lda, &inv, s, err);
+  int rc = run_rms_prep(x, ldx, gamma, M, K, eps, prep, &a, &lda, &inv, s, err, acc1, clear_bytes);
   if (rc) return rc;
   StreamProblem up;
   up.M = M;

@@ -82,11 +82,13 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int6
 
 // RMSNorm staging pass (rmsnorm_prep.cu): writes bf16(x * gamma) with leading
 // dimension staged_ld(K) and inv[m] = 1/sqrt(mean_k(x^2) + eps) into `ws`
-// (rms_prep_bytes(M, K) bytes, 256-byte aligned).
+// (rms_prep_bytes(M, K) bytes, 256-byte aligned). The same launch clears
+// `zero_bytes` bytes at `zero` (accumulators of the streamed GEMMs).
 int64_t staged_ld(int64_t k);
 size_t rms_prep_bytes(int64_t m, int64_t k);
 int run_rms_prep(const bf16* x, int64_t ldx, const bf16* gamma, int64_t M, int64_t K, float eps, void* ws,
-                 bf16** a_out, int64_t* lda_out, float** inv_out, cudaStream_t stream, std::string* err);
+                 bf16** a_out, int64_t* lda_out, float** inv_out, cudaStream_t stream, std::string* err,
+                 void* zero = nullptr, size_t zero_bytes = 0);
 
 // Device status word (per device): set by kernels whose bounded waits ran out.
 int* device_status_ptr(std::string* err);

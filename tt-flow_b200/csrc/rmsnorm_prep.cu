@@ -75,6 +75,57 @@ __global__ void __launch_bounds__(kWarps * 32) k_rms_prep(const bf16* __restrict
   }
 }
 
+// Few rows: a whole CTA per row so the row's loads are all in flight at once,
+// and CTAs past the last row clear `zero` (the streamed GEMMs' fp32
+// accumulators and counters) with 16-byte stores.
+constexpr int kRowThreads = 256;
+
+__global__ void __launch_bounds__(kRowThreads) k_rms_prep_rows(const bf16* __restrict__ x, int64_t ldx,
+                                                               const bf16* __restrict__ gamma, int M, int K,
+                                                               float eps, bf16* __restrict__ a, int64_t lda,
+                                                               float* __restrict__ inv, uint4* __restrict__ zero,
+                                                               int64_t zero_vecs) {
+  if (blockIdx.x >= M) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x - M) * kRowThreads;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x - M) * kRowThreads + threadIdx.x; i < zero_vecs; i += stride)
+      zero[i] = make_uint4(0u, 0u, 0u, 0u);
+    return;
+  }
+  const int64_t row = blockIdx.x;
+  const uint4* xv = reinterpret_cast<const uint4*>(x + row * ldx);
+  const int nchunk = K / 8;
+  uint64_t ss2 = 0;
+#pragma unroll 4
+  for (int c = threadIdx.x; c < nchunk; c += kRowThreads) {
+    const uint4 v = __ldg(xv + c);
+    ss2 = sq_acc_bf16x2(ss2, v.x);
+    ss2 = sq_acc_bf16x2(ss2, v.y);
+    ss2 = sq_acc_bf16x2(ss2, v.z);
+    ss2 = sq_acc_bf16x2(ss2, v.w);
+  }
+  float ss = __uint_as_float(static_cast<uint32_t>(ss2)) + __uint_as_float(static_cast<uint32_t>(ss2 >> 32));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  __shared__ float part[kRowThreads / 32];
+  __shared__ float s_inv;
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (int w = 0; w < kRowThreads / 32; ++w) t += part[w];
+    s_inv = 1.0f / sqrtf(t / static_cast<float>(K) + eps);
+    inv[row] = s_inv;
+  }
+  const uint4* gv = reinterpret_cast<const uint4*>(gamma);
+  uint4* av = reinterpret_cast<uint4*>(a + row * lda);
+#pragma unroll 4
+  for (int c = threadIdx.x; c < nchunk; c += kRowThreads) {
+    const uint4 v = __ldg(xv + c);
+    const uint4 g = __ldg(gv + c);
+    av[c] = make_uint4(mul_bf16x2(v.x, g.x), mul_bf16x2(v.y, g.y), mul_bf16x2(v.z, g.z), mul_bf16x2(v.w, g.w));
+  }
+}
+
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -88,12 +139,38 @@ size_t rms_prep_bytes(int64_t m, int64_t k) {
 }
 
 int run_rms_prep(const bf16* x, int64_t ldx, const bf16* gamma, int64_t M, int64_t K, float eps, void* ws,
-                 bf16** a_out, int64_t* lda_out, float** inv_out, cudaStream_t stream, std::string* err) {
+                 bf16** a_out, int64_t* lda_out, float** inv_out, cudaStream_t stream, std::string* err,
+                 void* zero, size_t zero_bytes) {
   const int64_t lda = staged_ld(K);
   bf16* a = static_cast<bf16*>(ws);
   const size_t abytes = (static_cast<size_t>(M) * lda * 2 + 255) & ~size_t(255);
   float* inv = reinterpret_cast<float*>(static_cast<char*>(ws) + abytes);
   const bool vec = K % 8 == 0 && ldx % 8 == 0 && al16(x) && al16(gamma) && al16(a);
+  *a_out = a;
+  *lda_out = lda;
+  *inv_out = inv;
+  if (vec && M <= 1024 && (zero_bytes % 16) == 0 && al16(zero)) {
+    // Few rows: one CTA per row, plus CTAs that clear `zero`.
+    const int64_t zvec = static_cast<int64_t>(zero_bytes / 16);
+    const int zblocks = zvec ? static_cast<int>(zvec / (kRowThreads * 8) + 1 < 512 ? zvec / (kRowThreads * 8) + 1 : 512)
+                             : 0;
+    k_rms_prep_rows<<<static_cast<int>(M) + zblocks, kRowThreads, 0, stream>>>(
+        x, ldx, gamma, static_cast<int>(M), static_cast<int>(K), eps, a, lda, inv, static_cast<uint4*>(zero), zvec);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      if (err) *err = std::string("rmsnorm staging launch: ") + cudaGetErrorString(e);
+      return -3;
+    }
+    count_launch();
+    return 0;
+  }
+  if (zero_bytes) {
+    const cudaError_t e = cudaMemsetAsync(zero, 0, zero_bytes, stream);
+    if (e != cudaSuccess) {
+      if (err) *err = std::string("accumulator clear: ") + cudaGetErrorString(e);
+      return -3;
+    }
+  }
   const int64_t blocks64 = (M + kWarps - 1) / kWarps;
   const int blocks = static_cast<int>(blocks64 < 65535 * 8 ? blocks64 : 65535 * 8);
   if (vec)
@@ -108,9 +185,6 @@ int run_rms_prep(const bf16* x, int64_t ldx, const bf16* gamma, int64_t M, int64
     return -3;
   }
   count_launch();
-  *a_out = a;
-  *lda_out = lda;
-  *inv_out = inv;
   return 0;
 }
 

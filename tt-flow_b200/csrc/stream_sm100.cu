@@ -286,15 +286,30 @@ __global__ void __launch_bounds__(256, 1)
         const int nf = nb * SBN + et;
         if (nf < p.N) {
           const float bias = (p.mode == kStreamFinishUp && p.bias) ? __bfloat162float(p.bias[nf]) : 0.0f;
-          for (int m = 0; m < p.M; ++m) {
-            float val = __ldcg(p.acc + static_cast<int64_t>(m) * p.N + nf);
-            if (p.mode == kStreamFinishUp) {
-              val = val * __ldg(p.col_scale + m) + bias;
-              val = p.gelu == kGeluErf ? gelu_erf(val) : (p.gelu == kGeluTanh ? gelu_tanh(val) : val);
-            } else {
-              val += __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ldr + nf]);
+          // Eight rows per step so their loads are in flight together.
+          for (int m0 = 0; m0 < p.M; m0 += 8) {
+            float val[8], add[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int m = m0 + j;
+              val[j] = m < p.M ? __ldcg(p.acc + static_cast<int64_t>(m) * p.N + nf) : 0.0f;
+              if (p.mode == kStreamFinishUp)
+                add[j] = m < p.M ? __ldg(p.col_scale + m) : 0.0f;
+              else
+                add[j] = m < p.M ? __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ldr + nf]) : 0.0f;
             }
-            p.out[static_cast<int64_t>(m) * p.ldo + nf] = __float2bfloat16_rn(val);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int m = m0 + j;
+              float v = val[j];
+              if (p.mode == kStreamFinishUp) {
+                v = v * add[j] + bias;
+                v = p.gelu == kGeluErf ? gelu_erf(v) : (p.gelu == kGeluTanh ? gelu_tanh(v) : v);
+              } else {
+                v += add[j];
+              }
+              if (m < p.M) p.out[static_cast<int64_t>(m) * p.ldo + nf] = __float2bfloat16_rn(v);
+            }
           }
         }
         epi_bar();
