@@ -37,9 +37,13 @@ import numpy as np  # noqa: E402
 
 METRIC = "fused RMSNorm+MatMul / MLP TFLOP/s & % bf16 tensor peak at 1/2/4/8 B200"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# Bytes moved by the dominant kernel per launch, from the ncu capture summarised
-# in profiles/ (dram__bytes_read.sum + dram__bytes_write.sum); None until captured.
-TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {}
+# DRAM bytes moved by the dominant kernel per launch (dram__bytes_read.sum +
+# dram__bytes_write.sum, averaged over the kernel's launches in one step), from the
+# ncu captures summarised in profiles/k_gemm_mlp_8192x4096x16384.md and
+# profiles/k_stream_decode_mlp_32x8192x28672.md.
+TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {
+    "mlp_8192x4096x16384": (604.663e6 + 245.780e6 + 1316.242e6 + 61.816e6) / 2,
+}
 
 
 def peaks():
