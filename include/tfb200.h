@@ -154,6 +154,20 @@ int tfb200_fused_mlp_noalloc(const tfb200_mat* x, const void* gamma, const tfb20
                              const tfb200_mat* w2, const tfb200_mat* residual, float eps, int gelu_mode,
                              tfb200_mat* y, void* stream);
 
+/* The tensixflow front end of this backend on IR text: parse the dialect
+ * subset of the fused path, apply `args` in order (the tensixflow-opt flags
+ * --tensixflow-device=b200, --tensixflow-fuse-rmsnorm-matmul,
+ * --tensixflow-plan-noc-sharding, --tensixflow-allocate-circular-buffers, or
+ * --tensixflow-to-json for the plan JSON of tensixflow-translate) and write the
+ * printed IR or JSON, NUL-terminated, to `out`. *needed (if not NULL) receives
+ * the size the output needs; TFB200_ENOSPC when `cap` is smaller. Host-only: no
+ * device is touched. Replaces tensixflow-opt's pass pipeline for these flags
+ * (FuseRmsnormMatmulPass.cpp:203-234, PlanNocShardingPass.cpp:135-304,
+ * AllocateCircularBuffersPass.cpp:63-104) and tensixflow-translate's
+ * --tensixflow-to-json (tensixflow-translate.cpp:75-222, 291-297), with the B200
+ * planner in place of the Tensix planner. */
+int tfb200_opt(const char* text, const char* args, char* out, size_t cap, size_t* needed);
+
 /* Device status word of the current device: TFB200_OK, or TFB200_ETIMEOUT if a
  * kernel's bounded wait ran out since the last clear. Synchronises the device. */
 int tfb200_device_status(void);

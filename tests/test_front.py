@@ -1,0 +1,146 @@
+"""The tensixflow front end on the B200 backend (CPU only).
+
+* The reference's own lit tests for the dialect, the verifiers and the fusion
+  passes run unchanged through `tfb200-opt` and FileCheck (when the reference
+  tree is present in this container; they are skipped elsewhere).
+* This backend's lit tests (tests/lit) pin the B200 planner's schedule and
+  emission attributes, device selection and the fused_mlp verifier.
+* The plan JSON matches the reference's plan schema (required keys, no extra
+  keys, JSON types, enums), through a digest of that schema committed in
+  tests/golden (tests/golden/make_schema_digest.py).
+* The planner's time model agrees with the measured kernels.
+"""
+
+import ctypes
+import json
+import subprocess
+from pathlib import Path
+
+import pytest
+
+import litrun
+
+ROOT = Path(__file__).resolve().parents[1]
+REF_TESTS = Path("/root/reference/test/Tensixflow")
+# Reference lit files whose RUN lines exercise what this backend implements
+# (parsing/printing, verifiers, fusion passes). plan_noc_sharding.mlir checks
+# n150 Tensix planner numbers, which the B200 planner replaces; the other files
+# test Tenstorrent lowering, TT-Metalium emission or TTIR import.
+REF_FILES = ["attrs.mlir", "dialect_parse.mlir", "smoke.mlir", "ops.mlir", "matmul.mlir", "rmsnorm.mlir",
+             "shape_inference.mlir", "fused_ops.mlir", "fuse_rmsnorm_matmul.mlir", "fuse_mlp.mlir",
+             "fusion_tracking.mlir"]
+
+
+@pytest.fixture(scope="module", autouse=True)
+def tool():
+    if not litrun.TOOL.exists():
+        subprocess.run(["make", "-C", str(ROOT / "tt-flow_b200"), "bin/tfb200-opt"], check=True, capture_output=True)
+    if litrun.filecheck() is None:
+        pytest.skip("FileCheck (shipped with triton) not available")
+    return litrun.TOOL
+
+
+@pytest.mark.parametrize("name", REF_FILES)
+def test_reference_lit_file(name):
+    path = REF_TESTS / name
+    if not path.exists():
+        pytest.skip("reference tree not present")
+    r = litrun.run_file(path)
+    assert r["ran"] > 0
+    assert not r["failed"], r["failed"]
+
+
+@pytest.mark.parametrize("path", sorted((ROOT / "tests" / "lit").glob("*.mlir")), ids=lambda p: p.name)
+def test_b200_lit_file(path):
+    r = litrun.run_file(path)
+    assert r["ran"] > 0 and not r["skipped"], r
+    assert not r["failed"], r["failed"]
+
+
+def _opt(text, *flags):
+    p = subprocess.run([str(litrun.TOOL), *flags], input=text, capture_output=True, text=True)
+    return p.returncode, p.stdout, p.stderr
+
+
+def _check(value, schema, where="plan"):
+    t = schema.get("type")
+    pytypes = {"object": dict, "array": list, "string": str, "boolean": bool, "number": (int, float),
+               "integer": int}
+    if t:
+        assert isinstance(value, pytypes[t]) and not (t == "integer" and isinstance(value, bool)), where
+    if "enum" in schema:
+        assert value in schema["enum"], (where, value)
+    if t == "object":
+        for k in schema["required"]:
+            assert k in value, f"{where}: missing {k}"
+        if schema["additional"] is False:
+            extra = set(value) - set(schema["properties"])
+            assert not extra, f"{where}: unexpected keys {extra}"
+        for k, v in value.items():
+            if k in schema["properties"]:
+                _check(v, schema["properties"][k], f"{where}.{k}")
+    if t == "array" and "items" in schema:
+        for i, v in enumerate(value):
+            _check(v, schema["items"], f"{where}[{i}]")
+
+
+@pytest.mark.parametrize("lit", ["b200_plan_rmsnorm_matmul.mlir", "b200_plan_mlp.mlir", "b200_plan_decode.mlir"])
+def test_plan_json_matches_reference_schema(lit):
+    text = (ROOT / "tests" / "lit" / lit).read_text()
+    rc, out, err = _opt(text, "--tensixflow-fuse-rmsnorm-matmul", "--tensixflow-to-json")
+    assert rc == 0, err
+    plan = json.loads(out)
+    schema = json.loads((ROOT / "tests" / "golden" / "plan_schema_digest.json").read_text())
+    _check(plan, schema)
+    assert plan["device"]["name"] == "b200" and plan["emission"]["fused_feasible"] is True
+    assert plan["noc"]["multicast_bytes"] == 0
+
+
+def test_unfusable_graph_plans_unfused():
+    text = """tensixflow.func @lone(%a: tensor<4096x4096xbf16>, %b: tensor<4096x4096xbf16>) -> tensor<4096x4096xbf16> {
+  %0 = tensixflow.matmul %a, %b : tensor<4096x4096xbf16> x tensor<4096x4096xbf16> -> tensor<4096x4096xbf16>
+  tensixflow.return %0 : tensor<4096x4096xbf16>
+}"""
+    rc, out, err = _opt(text, "--tensixflow-fuse-rmsnorm-matmul", "--tensixflow-to-json")
+    assert rc == 0, err
+    plan = json.loads(out)
+    assert plan["fusion"] == "none" and plan["estimated_dram_reads_saved"] == 0
+    assert plan["perf"]["bottleneck"] == "compute"
+
+
+def test_parse_errors_are_reported():
+    rc, out, err = _opt("tensixflow.func @f(%a: tensor<4xbf16>) -> tensor<4xbf16> {\n  %0 = tensixflow.gelu %b : tensor<4xbf16>\n}")
+    assert rc != 0 and "undefined value" in err
+
+
+def test_c_abi_matches_tool():
+    from tfb200 import _lib as L
+
+    lib = L.lib()
+    text = (ROOT / "tests" / "lit" / "b200_plan_mlp.mlir").read_text()
+    flags = "--tensixflow-fuse-rmsnorm-matmul --tensixflow-plan-noc-sharding --tensixflow-allocate-circular-buffers"
+    need = ctypes.c_size_t(0)
+    assert lib.tfb200_opt(text.encode(), flags.encode(), None, 0, ctypes.byref(need)) == L.TFB200_ENOSPC
+    buf = ctypes.create_string_buffer(need.value)
+    assert lib.tfb200_opt(text.encode(), flags.encode(), buf, need.value, None) == L.TFB200_OK
+    rc, out, _ = _opt(text, *flags.split())
+    assert rc == 0 and buf.value.decode() == out
+    assert lib.tfb200_opt(b"tensixflow.func @f(", b"", None, 0, None) == L.TFB200_EINVAL
+    assert b"error" in lib.tfb200_last_error()
+
+
+# Measured on B200 with CUDA events (bench.py): fused MLP 8192x4096x16384 1.678 ms
+# per step, fused RMSNorm+QKV 8192x4096x6144 0.339 ms, decode MLP 32x8192x28672
+# 0.183 ms per step.
+MEASURED_S = {"b200_plan_mlp.mlir": 1.678e-3, "b200_plan_rmsnorm_matmul.mlir": 0.339e-3,
+              "b200_plan_decode.mlir": 0.183e-3}
+
+
+@pytest.mark.parametrize("lit", sorted(MEASURED_S))
+def test_time_model_tracks_measurement(lit):
+    text = (ROOT / "tests" / "lit" / lit).read_text()
+    rc, out, err = _opt(text, "--tensixflow-fuse-rmsnorm-matmul", "--tensixflow-to-json")
+    assert rc == 0, err
+    plan = json.loads(out)
+    est_s = plan["perf"]["est_cycles"] / 1.965e9
+    assert abs(est_s / MEASURED_S[lit] - 1.0) < 0.15, (est_s, MEASURED_S[lit])
