@@ -31,7 +31,9 @@
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
+#include <string>
 
 #include "internal.h"
 #include "sm100_ptx.cuh"
@@ -92,9 +94,11 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm
 }
 
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+// tanh form of GELU with the hardware tanh (tanh.approx.f32, relative error
+// about 2^-11): well inside the bf16 rounding (2^-9) of the value it produces.
 __device__ __forceinline__ float gelu_tanh(float x) {
-  const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
-  return 0.5f * x * (1.0f + tanhf(u));
+  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+  return 0.5f * x * (1.0f + tanh_approx(u));
 }
 
 __device__ __forceinline__ void raise_abort(SmemCtl* ctl, int* status) {
@@ -109,6 +113,74 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, SmemCtl
   if (!ok && (threadIdx.x & 31) == 0) raise_abort(ctl, p.status);
   return ok;
 }
+
+// Row scale, bias, GELU and residual on 32 accumulator columns of one row, then
+// bf16 round and store (columns col0 .. col0+31 of `row`).
+__device__ __forceinline__ void epilogue_chunk(const KParams& p, const uint32_t (&v)[32], float scale, int64_t row,
+                                               int col0) {
+  float f[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * scale;
+  const bool full = p.vec_ok && (col0 + 32 <= p.N);
+  if (p.bias) {
+    if (full) {
+      const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint4 b = __ldg(bp + u);
+        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          f[u * 8 + 2 * e] += bf16_lo(bw[e]);
+          f[u * 8 + 2 * e + 1] += bf16_hi(bw[e]);
+        }
+      }
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) f[j] += __bfloat162float(p.bias[col0 + j]);
+    }
+  }
+  if (p.gelu == kGeluErf) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = gelu_erf(f[j]);
+  } else if (p.gelu == kGeluTanh) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = gelu_tanh(f[j]);
+  }
+  if (p.residual) {
+    const bf16* rp = p.residual + row * p.ldr + col0;
+    if (full) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint4 b = *reinterpret_cast<const uint4*>(rp + u * 8);
+        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          f[u * 8 + 2 * e] += bf16_lo(bw[e]);
+          f[u * 8 + 2 * e + 1] += bf16_hi(bw[e]);
+        }
+      }
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) f[j] += __bfloat162float(rp[j]);
+    }
+  }
+  bf16* cp = p.C + row * p.ldc + col0;
+  if (full) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      uint4 o;
+      o.x = pack_bf16(f[u * 8 + 0], f[u * 8 + 1]);
+      o.y = pack_bf16(f[u * 8 + 2], f[u * 8 + 3]);
+      o.z = pack_bf16(f[u * 8 + 4], f[u * 8 + 5]);
+      o.w = pack_bf16(f[u * 8 + 6], f[u * 8 + 7]);
+      *reinterpret_cast<uint4*>(cp + u * 8) = o;
+    }
+  } else {
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < p.N) cp[j] = __float2bfloat16_rn(f[j]);
+  }
+      }
 
 template <bool MANUAL>
 struct Roles {
@@ -169,37 +241,37 @@ __global__ void __launch_bounds__(Roles<MANUAL>::kThreads, 1)
       uint32_t armed = 0, armed_phase = 0;  // stages with loads in flight (for the drain)
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        int tm, tn;
-        tile_coords(t, num_m, num_n, tm, tn);
-        for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(smem_u32(&ctl->empty[stage]), phase ^ 1u, &ctl->abort, p.timeout_ns)) {
-            raise_abort(ctl, p.status);
-            ok = false;
-            break;
-          }
-          const uint32_t fb = smem_u32(&ctl->full[stage]);
-          mbar_arrive_expect_tx(fb, A_STAGE_BYTES + B_STAGE_BYTES);
-          tma_load_2d(smem_u32(sA + stage * A_STAGE_BYTES), &tmA, fb, kb * BK, tm * BM);
+  int tm, tn;
+  tile_coords(t, num_m, num_n, tm, tn);
+  for (int kb = 0; kb < kblocks; ++kb) {
+    if (!mbar_wait(smem_u32(&ctl->empty[stage]), phase ^ 1u, &ctl->abort, p.timeout_ns)) {
+      raise_abort(ctl, p.status);
+      ok = false;
+      break;
+    }
+    const uint32_t fb = smem_u32(&ctl->full[stage]);
+    mbar_arrive_expect_tx(fb, A_STAGE_BYTES + B_STAGE_BYTES);
+    tma_load_2d(smem_u32(sA + stage * A_STAGE_BYTES), &tmA, fb, kb * BK, tm * BM);
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d(smem_u32(sB + stage * B_STAGE_BYTES + j * 8192), &tmB, fb, tn * BN + j * 64, kb * BK);
-          armed |= 1u << stage;
-          armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
+    for (int j = 0; j < BN / 64; ++j)
+      tma_load_2d(smem_u32(sB + stage * B_STAGE_BYTES + j * 8192), &tmB, fb, tn * BN + j * 64, kb * BK);
+    armed |= 1u << stage;
+    armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+    if (++stage == STAGES) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
       }
       if (!ok) {
-        // Let the copies already issued land before the CTA's shared memory goes away.
-        for (int s = 0; s < STAGES; ++s)
-          if (armed & (1u << s)) {
-            const uint64_t t0 = global_ns();
-            while (!mbar_test(smem_u32(&ctl->full[s]), (armed_phase >> s) & 1u) &&
-                   global_ns() - t0 < p.timeout_ns) {
-            }
-          }
+  // Let the copies already issued land before the CTA's shared memory goes away.
+  for (int s = 0; s < STAGES; ++s)
+    if (armed & (1u << s)) {
+      const uint64_t t0 = global_ns();
+      while (!mbar_test(smem_u32(&ctl->full[s]), (armed_phase >> s) & 1u) &&
+             global_ns() - t0 < p.timeout_ns) {
+      }
+    }
       }
     }
   } else if (warp == 1) {
@@ -211,38 +283,38 @@ __global__ void __launch_bounds__(Roles<MANUAL>::kThreads, 1)
       bool ok = true;
       int i = 0;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++i) {
-        const int acc = i & 1;
-        const uint32_t use = static_cast<uint32_t>(i >> 1);
-        if (!mbar_wait(smem_u32(&ctl->tempty[acc]), (use & 1u) ^ 1u, &ctl->abort, p.timeout_ns)) {
-          raise_abort(ctl, p.status);
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < kblocks && ok; ++kb) {
-          if (!mbar_wait(smem_u32(&ctl->full[stage]), phase, &ctl->abort, p.timeout_ns)) {
-            raise_abort(ctl, p.status);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + stage * A_STAGE_BYTES);
-          const uint32_t b0 = smem_u32(sB + stage * B_STAGE_BYTES);
+  const int acc = i & 1;
+  const uint32_t use = static_cast<uint32_t>(i >> 1);
+  if (!mbar_wait(smem_u32(&ctl->tempty[acc]), (use & 1u) ^ 1u, &ctl->abort, p.timeout_ns)) {
+    raise_abort(ctl, p.status);
+    ok = false;
+    break;
+  }
+  tc_fence_after();
+  const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+  for (int kb = 0; kb < kblocks && ok; ++kb) {
+    if (!mbar_wait(smem_u32(&ctl->full[stage]), phase, &ctl->abort, p.timeout_ns)) {
+      raise_abort(ctl, p.status);
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    const uint32_t a0 = smem_u32(sA + stage * A_STAGE_BYTES);
+    const uint32_t b0 = smem_u32(sB + stage * B_STAGE_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(b0 + k * 2048, 8192, 1024);
-            mma_bf16(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
-          }
-          if (!ok) break;
-          mma_commit(smem_u32(&ctl->empty[stage]));
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-        if (ok) mma_commit(smem_u32(&ctl->tfull[acc]));
+    for (int k = 0; k < BK / 16; ++k) {
+      const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
+      const uint64_t bd = sdesc_sw128(b0 + k * 2048, 8192, 1024);
+      mma_bf16(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+    }
+    if (!ok) break;
+    mma_commit(smem_u32(&ctl->empty[stage]));
+    if (++stage == STAGES) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
+  if (ok) mma_commit(smem_u32(&ctl->tfull[acc]));
       }
       // Wait until every MMA this thread issued has finished (TMEM is freed below).
       mma_commit(smem_u32(&ctl->drain));
@@ -265,76 +337,13 @@ __global__ void __launch_bounds__(Roles<MANUAL>::kThreads, 1)
       const int64_t row = static_cast<int64_t>(tm) * BM + r;
       const float scale = (p.row_scale && row < p.M) ? __ldg(p.row_scale + row) : 1.0f;
       for (int c = 0; c < BN / 32; ++c) {
-        const int col0 = tn * BN + c * 32;
-        if (col0 >= p.N) break;  // warp-uniform
-        uint32_t v[32];
-        tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + c * 32),
-                       v);
-        tmem_wait_ld();
-        if (row < p.M) {
-          float f[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * scale;
-          const bool full = p.vec_ok && (col0 + 32 <= p.N);
-          if (p.bias) {
-            if (full) {
-              const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0);
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const uint4 b = __ldg(bp + u);
-                const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  f[u * 8 + 2 * e] += bf16_lo(bw[e]);
-                  f[u * 8 + 2 * e + 1] += bf16_hi(bw[e]);
-                }
-              }
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < p.N) f[j] += __bfloat162float(p.bias[col0 + j]);
-            }
-          }
-          if (p.gelu == kGeluErf) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) f[j] = gelu_erf(f[j]);
-          } else if (p.gelu == kGeluTanh) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) f[j] = gelu_tanh(f[j]);
-          }
-          if (p.residual) {
-            const bf16* rp = p.residual + row * p.ldr + col0;
-            if (full) {
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const uint4 b = *reinterpret_cast<const uint4*>(rp + u * 8);
-                const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  f[u * 8 + 2 * e] += bf16_lo(bw[e]);
-                  f[u * 8 + 2 * e + 1] += bf16_hi(bw[e]);
-                }
-              }
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < p.N) f[j] += __bfloat162float(rp[j]);
-            }
-          }
-          bf16* cp = p.C + row * p.ldc + col0;
-          if (full) {
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              uint4 o;
-              o.x = pack_bf16(f[u * 8 + 0], f[u * 8 + 1]);
-              o.y = pack_bf16(f[u * 8 + 2], f[u * 8 + 3]);
-              o.z = pack_bf16(f[u * 8 + 4], f[u * 8 + 5]);
-              o.w = pack_bf16(f[u * 8 + 6], f[u * 8 + 7]);
-              *reinterpret_cast<uint4*>(cp + u * 8) = o;
-            }
-          } else {
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < p.N) cp[j] = __float2bfloat16_rn(f[j]);
-          }
-        }
+  const int col0 = tn * BN + c * 32;
+  if (col0 >= p.N) break;  // warp-uniform
+  uint32_t v[32];
+  tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + c * 32),
+                 v);
+  tmem_wait_ld();
+  if (row < p.M) epilogue_chunk(p, v, scale, row, col0);
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl->tempty[acc]));
@@ -349,51 +358,51 @@ __global__ void __launch_bounds__(Roles<MANUAL>::kThreads, 1)
       int tm, tn;
       tile_coords(t, num_m, num_n, tm, tn);
       for (int kb = 0; kb < kblocks; ++kb) {
-        if (!warp_wait(smem_u32(&ctl->empty[stage]), phase ^ 1u, ctl, p)) {
-          ok = false;
-          break;
-        }
-        // A: thread tid owns row tid of the tile.
-        {
-          const int64_t gm = static_cast<int64_t>(tm) * BM + tid;
-          uint8_t* rowp = sA + stage * A_STAGE_BYTES + tid * 128;
-          for (int c = 0; c < 8; ++c) {
-            uint32_t w[4];
-            for (int e = 0; e < 4; ++e) {
-              const int k = kb * BK + c * 8 + 2 * e;
-              float lo = 0.f, hi = 0.f;
-              if (gm < p.M && k < p.K) lo = __bfloat162float(p.A[gm * p.lda + k]);
-              if (gm < p.M && k + 1 < p.K) hi = __bfloat162float(p.A[gm * p.lda + k + 1]);
-              w[e] = pack_bf16(lo, hi);
-            }
-            *reinterpret_cast<uint4*>(rowp + ((c ^ (tid & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
-        }
-        // B: thread tid owns k-row tid/2 and 128 of the 256 columns.
-        {
-          const int kr = tid >> 1;
-          const int64_t gk = static_cast<int64_t>(kb) * BK + kr;
-          for (int cc = 0; cc < 16; ++cc) {
-            const int nl = (tid & 1) * 128 + cc * 8;
-            uint32_t w[4];
-            for (int e = 0; e < 4; ++e) {
-              const int64_t n = static_cast<int64_t>(tn) * BN + nl + 2 * e;
-              float lo = 0.f, hi = 0.f;
-              if (gk < p.K && n < p.N) lo = __bfloat162float(p.B[gk * p.ldb + n]);
-              if (gk < p.K && n + 1 < p.N) hi = __bfloat162float(p.B[gk * p.ldb + n + 1]);
-              w[e] = pack_bf16(lo, hi);
-            }
-            uint8_t* dst = sB + stage * B_STAGE_BYTES + (nl >> 6) * 8192 + kr * 128 +
-                           ((((nl & 63) >> 3) ^ (kr & 7)) << 4);
-            *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(smem_u32(&ctl->full[stage]));
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
+  if (!warp_wait(smem_u32(&ctl->empty[stage]), phase ^ 1u, ctl, p)) {
+    ok = false;
+    break;
+  }
+  // A: thread tid owns row tid of the tile.
+  {
+    const int64_t gm = static_cast<int64_t>(tm) * BM + tid;
+    uint8_t* rowp = sA + stage * A_STAGE_BYTES + tid * 128;
+    for (int c = 0; c < 8; ++c) {
+      uint32_t w[4];
+      for (int e = 0; e < 4; ++e) {
+        const int k = kb * BK + c * 8 + 2 * e;
+        float lo = 0.f, hi = 0.f;
+        if (gm < p.M && k < p.K) lo = __bfloat162float(p.A[gm * p.lda + k]);
+        if (gm < p.M && k + 1 < p.K) hi = __bfloat162float(p.A[gm * p.lda + k + 1]);
+        w[e] = pack_bf16(lo, hi);
+      }
+      *reinterpret_cast<uint4*>(rowp + ((c ^ (tid & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  // B: thread tid owns k-row tid/2 and 128 of the 256 columns.
+  {
+    const int kr = tid >> 1;
+    const int64_t gk = static_cast<int64_t>(kb) * BK + kr;
+    for (int cc = 0; cc < 16; ++cc) {
+      const int nl = (tid & 1) * 128 + cc * 8;
+      uint32_t w[4];
+      for (int e = 0; e < 4; ++e) {
+        const int64_t n = static_cast<int64_t>(tn) * BN + nl + 2 * e;
+        float lo = 0.f, hi = 0.f;
+        if (gk < p.K && n < p.N) lo = __bfloat162float(p.B[gk * p.ldb + n]);
+        if (gk < p.K && n + 1 < p.N) hi = __bfloat162float(p.B[gk * p.ldb + n + 1]);
+        w[e] = pack_bf16(lo, hi);
+      }
+      uint8_t* dst = sB + stage * B_STAGE_BYTES + (nl >> 6) * 8192 + kr * 128 +
+                     ((((nl & 63) >> 3) ^ (kr & 7)) << 4);
+      *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  fence_proxy_async_smem();
+  mbar_arrive(smem_u32(&ctl->full[stage]));
+  if (++stage == STAGES) {
+    stage = 0;
+    phase ^= 1u;
+  }
       }
     }
   }
@@ -403,6 +412,225 @@ __global__ void __launch_bounds__(Roles<MANUAL>::kThreads, 1)
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+
+// ----------------------------------------------------------- CTA-pair kernel
+//
+// Same contract as k_gemm, with a 256 x 256 output tile per pair of CTAs
+// (cluster of 2) and tcgen05.mma.cta_group::2: each CTA stages its own 128 rows
+// of A and its own 128 columns of B per 64-deep k block (16 + 16 KiB), the
+// leader CTA issues one 256x256x16 MMA over both CTAs' shared memory, and each
+// CTA's TMEM receives its 128 rows of the fp32 accumulator. Halving the B bytes
+// staged per CTA frees shared memory for six stages instead of four.
+// Barriers: both CTAs' TMA loads complete on the leader's `full` barrier (armed
+// by the leader with both CTAs' bytes); the leader's MMA thread signals each
+// CTA's `empty` and `tfull` barrier; both CTAs' epilogue warps arrive on the
+// leader's `tempty` barrier. Every wait is bounded.
+constexpr int PSTAGES = 6;
+constexpr int PBM = 2 * BM;                       // rows per pair tile
+constexpr uint32_t PB_STAGE_BYTES = BM * BK * 2;  // this CTA's 128 of the 256 B columns
+
+struct PairCtl {
+  uint64_t full[PSTAGES];
+  uint64_t empty[PSTAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t pair_smem_bytes() {
+  return 1024 + PSTAGES * (A_STAGE_BYTES + PB_STAGE_BYTES) + sizeof(PairCtl);
+}
+
+__device__ __forceinline__ void raise_abort_pair(PairCtl* ctl, int* status) {
+  ctl->abort = 1;
+  atomicExch(status, kDevTimeout);
+}
+
+__global__ void __launch_bounds__(256, 1)
+    k_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const KParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + PSTAGES * A_STAGE_BYTES;
+  PairCtl* ctl = reinterpret_cast<PairCtl*>(sB + PSTAGES * PB_STAGE_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PSTAGES; ++s) {
+      mbar_init(smem_u32(&ctl->full[s]), 1);
+      mbar_init(smem_u32(&ctl->empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&ctl->tfull[b]), 1);
+      mbar_init(smem_u32(&ctl->tempty[b]), 8);  // 4 epilogue warps in each CTA
+    }
+    mbar_init(smem_u32(&ctl->drain), 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(smem_u32(&ctl->tmem_base), TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem_base = ctl->tmem_base;
+
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int num_m = (p.M + PBM - 1) / PBM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int total = num_m * num_n;
+  const int kblocks = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < total && ok; t += npairs) {
+        int tm, tn;
+        tile_coords(t, num_m, num_n, tm, tn);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(smem_u32(&ctl->empty[stage]), phase ^ 1u, &ctl->abort, p.timeout_ns)) {
+            raise_abort_pair(ctl, p.status);
+            ok = false;
+            break;
+          }
+          const uint32_t fb = mapa_shared(smem_u32(&ctl->full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(smem_u32(&ctl->full[stage]), 2 * (A_STAGE_BYTES + PB_STAGE_BYTES));
+          tma_load_2d_pair(smem_u32(sA + stage * A_STAGE_BYTES), &tmA, fb, kb * BK,
+                           tm * PBM + static_cast<int>(rank) * BM);
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            tma_load_2d_pair(smem_u32(sB + stage * PB_STAGE_BYTES + j * 8192), &tmB, fb,
+                             tn * BN + static_cast<int>(rank) * 128 + j * 64, kb * BK);
+          if (++stage == PSTAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Copies already issued land within microseconds; give them time before
+        // the cluster tears down.
+        const uint64_t t0 = global_ns();
+        while (global_ns() - t0 < 1000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------- MMA issuer (leader)
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_bf16(PBM, BN, false, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int i = 0;
+      for (int t = pair; t < total && ok; t += npairs, ++i) {
+        const int acc = i & 1;
+        const uint32_t use = static_cast<uint32_t>(i >> 1);
+        if (!mbar_wait(smem_u32(&ctl->tempty[acc]), (use & 1u) ^ 1u, &ctl->abort, p.timeout_ns)) {
+          raise_abort_pair(ctl, p.status);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < kblocks && ok; ++kb) {
+          if (!mbar_wait(smem_u32(&ctl->full[stage]), phase, &ctl->abort, p.timeout_ns)) {
+            raise_abort_pair(ctl, p.status);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_STAGE_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * PB_STAGE_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b0 + k * 2048, 8192, 1024);
+            mma_bf16_pair(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          const uint32_t e = smem_u32(&ctl->empty[stage]);
+          mma_commit_pair(e);
+          mma_commit_pair(mapa_shared(e, 1));
+          if (++stage == PSTAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) {
+          const uint32_t f = smem_u32(&ctl->tfull[acc]);
+          mma_commit_pair(f);
+          mma_commit_pair(mapa_shared(f, 1));
+        }
+      }
+      mma_commit_pair(smem_u32(&ctl->drain));
+      const uint64_t t0 = global_ns();
+      while (!mbar_test(smem_u32(&ctl->drain), 0) && global_ns() - t0 < p.timeout_ns) {
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------- epilogue (both CTAs)
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    int i = 0;
+    for (int t = pair; t < total; t += npairs, ++i) {
+      int tm, tn;
+      tile_coords(t, num_m, num_n, tm, tn);
+      const int acc = i & 1;
+      const uint32_t use = static_cast<uint32_t>(i >> 1);
+      bool ok = mbar_wait(smem_u32(&ctl->tfull[acc]), use & 1u, &ctl->abort, p.timeout_ns);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0) raise_abort_pair(ctl, p.status);
+        break;
+      }
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(tm) * PBM + static_cast<int64_t>(rank) * BM + r;
+      const float scale = (p.row_scale && row < p.M) ? __ldg(p.row_scale + row) : 1.0f;
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = tn * BN + c * 32;
+        if (col0 >= p.N) break;  // warp-uniform
+        uint32_t v[32];
+        tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + c * 32),
+                       v);
+        tmem_wait_ld();
+        if (row < p.M) epilogue_chunk(p, v, scale, row, col0);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        const uint32_t te = smem_u32(&ctl->tempty[acc]);
+        if (leader)
+          mbar_arrive(te);
+        else
+          mbar_arrive_cluster(mapa_shared(te, 0));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still touch its barriers or shared memory
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -472,7 +700,82 @@ int launch(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int 
   return 0;
 }
 
+int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int pair_tiles, cudaStream_t s,
+                std::string* err) {
+  static bool attr_set[64] = {};
+  static int max_clusters[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const size_t smem = pair_smem_bytes();
+  if (dev < 0 || dev >= 64) {
+    if (err) *err = "device index out of range";
+    return -3;
+  }
+  if (!attr_set[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(k_gemm_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemm_pair, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+    if (e != cudaSuccess) {
+      if (err) *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+      return -3;
+    }
+    // Persistent pairs: launch no more clusters than can be resident at once.
+    cudaLaunchConfig_t q{};
+    q.gridDim = dim3(static_cast<unsigned>(sm_count()), 1, 1);
+    q.blockDim = dim3(256, 1, 1);
+    q.dynamicSmemBytes = smem;
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = 2;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = 1;
+    q.attrs = qa;
+    q.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, k_gemm_pair, &q);
+    if (e != cudaSuccess || n <= 0) {
+      if (err) *err = std::string("cudaOccupancyMaxActiveClusters: ") + cudaGetErrorString(e);
+      return -3;
+    }
+    max_clusters[dev] = n;
+    attr_set[dev] = true;
+  }
+  const int pairs = pair_tiles < max_clusters[dev] ? pair_tiles : max_clusters[dev];
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_pair, ta, tb, kp);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    if (err) *err = std::string("pair gemm launch: ") + cudaGetErrorString(e);
+    return -3;
+  }
+  count_launch();
+  return 0;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Kernel choice for TMA-describable operands: the CTA-pair kernel unless
+// TFB200_GEMM_KERNEL=single, or when the problem has too few rows to fill a
+// 256-row pair tile.
+bool use_pair(int64_t M) {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* v = std::getenv("TFB200_GEMM_KERNEL");
+    mode = (v && std::string(v) == "single") ? 0 : 1;
+  }
+  return mode == 1 && M > BM;
+}
 
 }  // namespace
 
@@ -516,6 +819,10 @@ int run_gemm(const GemmProblem& g, cudaStream_t stream, std::string* err) {
   if (tma_ok) {
     if (!make_map(&ta, g.A, g.M, g.K, g.lda, BM, err)) return -3;
     if (!make_map(&tb, g.B, g.K, g.N, g.ldb, BK, err)) return -3;
+    if (use_pair(g.M)) {
+      const int pair_tiles = static_cast<int>(((g.M + PBM - 1) / PBM) * ((g.N + BN - 1) / BN));
+      return launch_pair(kp, ta, tb, pair_tiles, stream, err);
+    }
     return launch<false>(kp, ta, tb, grid, stream, err);
   }
   return launch<true>(kp, ta, tb, grid, stream, err);
