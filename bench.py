@@ -42,7 +42,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # ncu captures summarised in profiles/k_gemm_mlp_8192x4096x16384.md and
 # profiles/k_stream_decode_mlp_32x8192x28672.md.
 TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {
-    "mlp_8192x4096x16384": (604.663e6 + 245.780e6 + 1316.242e6 + 61.816e6) / 2,
+    "mlp_8192x4096x16384": (416.845e6 + 249.460e6 + 1527.116e6 + 64.395e6) / 2,
 }
 
 
@@ -365,7 +365,7 @@ def run_ours(args) -> int:
         peak = pk["bf16_tflops_sustained"] if sustained else pk["bf16_tflops"]
         per_gpu = flops_step / (ms_step * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s", "frac": per_gpu / peak,
-                "traffic": TRAFFIC_BYTES_PER_LAUNCH.get(name), "kernel": "k_gemm (persistent tcgen05 GEMM)",
+                "traffic": TRAFFIC_BYTES_PER_LAUNCH.get(name), "kernel": "k_gemm_pair (persistent cta_group::2 tcgen05 GEMM)",
                 "launches_per_step": launches_per_step,
                 "peak_source": f"{pk_src} {'sustained' if sustained else 'burst'} bf16 (MEASURED_PEAKS.json)"
                 if pk_src == "measured" else "fallback"}
