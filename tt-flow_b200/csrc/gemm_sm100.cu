@@ -64,7 +64,8 @@ struct KParams {
   int gelu;
   const bf16* residual;
   int64_t ldr;
-  int vec_ok;  // C / residual / bias allow 16-byte accesses
+  int vec_ok;     // C / residual / bias allow 16-byte accesses
+  int tma_store;  // the pair kernel stores C through shared memory with TMA
   int* status;
   uint64_t timeout_ns;
 };
@@ -114,11 +115,10 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, SmemCtl
   return ok;
 }
 
-// Row scale, bias, GELU and residual on 32 accumulator columns of one row, then
-// bf16 round and store (columns col0 .. col0+31 of `row`).
-__device__ __forceinline__ void epilogue_chunk(const KParams& p, const uint32_t (&v)[32], float scale, int64_t row,
-                                               int col0) {
-  float f[32];
+// Row scale, bias, GELU and residual on 32 accumulator columns of one row
+// (columns col0 .. col0+31 of `row`), in fp32.
+__device__ __forceinline__ void epilogue_values(const KParams& p, const uint32_t (&v)[32], float scale, int64_t row,
+                                                int col0, float (&f)[32]) {
 #pragma unroll
   for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * scale;
   const bool full = p.vec_ok && (col0 + 32 <= p.N);
@@ -165,6 +165,14 @@ __device__ __forceinline__ void epilogue_chunk(const KParams& p, const uint32_t 
         if (col0 + j < p.N) f[j] += __bfloat162float(rp[j]);
     }
   }
+}
+
+// epilogue_values, then bf16 round and direct 16-byte stores.
+__device__ __forceinline__ void epilogue_chunk(const KParams& p, const uint32_t (&v)[32], float scale, int64_t row,
+                                               int col0) {
+  float f[32];
+  epilogue_values(p, v, scale, row, col0, f);
+  const bool full = p.vec_ok && (col0 + 32 <= p.N);
   bf16* cp = p.C + row * p.ldc + col0;
   if (full) {
 #pragma unroll
@@ -180,7 +188,7 @@ __device__ __forceinline__ void epilogue_chunk(const KParams& p, const uint32_t 
     for (int j = 0; j < 32; ++j)
       if (col0 + j < p.N) cp[j] = __float2bfloat16_rn(f[j]);
   }
-      }
+}
 
 template <bool MANUAL>
 struct Roles {
@@ -442,8 +450,12 @@ struct PairCtl {
   int abort;
 };
 
+// Epilogue staging for TMA stores: per epilogue warp two 32 x 32 bf16 buffers.
+constexpr uint32_t C_STAGE_BYTES = 32 * 32 * 2;
+constexpr uint32_t C_STAGING_BYTES = 4 * 2 * C_STAGE_BYTES;
+
 constexpr size_t pair_smem_bytes() {
-  return 1024 + PSTAGES * (A_STAGE_BYTES + PB_STAGE_BYTES) + sizeof(PairCtl);
+  return 1024 + PSTAGES * (A_STAGE_BYTES + PB_STAGE_BYTES) + C_STAGING_BYTES + sizeof(PairCtl);
 }
 
 __device__ __forceinline__ void raise_abort_pair(PairCtl* ctl, int* status) {
@@ -452,13 +464,15 @@ __device__ __forceinline__ void raise_abort_pair(PairCtl* ctl, int* status) {
 }
 
 __global__ void __launch_bounds__(256, 1)
-    k_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const KParams p) {
+    k_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, const KParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sB = smem + PSTAGES * A_STAGE_BYTES;
-  PairCtl* ctl = reinterpret_cast<PairCtl*>(sB + PSTAGES * PB_STAGE_BYTES);
+  uint8_t* sC = sB + PSTAGES * PB_STAGE_BYTES;
+  PairCtl* ctl = reinterpret_cast<PairCtl*>(sC + C_STAGING_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -479,6 +493,7 @@ __global__ void __launch_bounds__(256, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (p.tma_store) tma_prefetch_desc(&tmC);
   }
   if (warp == 2) {
     tmem_alloc_pair(smem_u32(&ctl->tmem_base), TMEM_COLS);
@@ -602,16 +617,47 @@ __global__ void __launch_bounds__(256, 1)
         break;
       }
       tc_fence_after();
-      const int64_t row = static_cast<int64_t>(tm) * PBM + static_cast<int64_t>(rank) * BM + r;
+      const int64_t row0 = static_cast<int64_t>(tm) * PBM + static_cast<int64_t>(rank) * BM + q * 32;
+      const int64_t row = row0 + lane;
       const float scale = (p.row_scale && row < p.M) ? __ldg(p.row_scale + row) : 1.0f;
       for (int c = 0; c < BN / 32; ++c) {
         const int col0 = tn * BN + c * 32;
-        if (col0 >= p.N) break;  // warp-uniform
+        if (col0 >= p.N || row0 >= p.M) break;  // warp-uniform: nothing of this block is in the matrix
         uint32_t v[32];
         tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + c * 32),
                        v);
         tmem_wait_ld();
-        if (row < p.M) epilogue_chunk(p, v, scale, row, col0);
+        if (!p.tma_store) {
+          if (row < p.M) epilogue_chunk(p, v, scale, row, col0);
+          continue;
+        }
+        // Stage the warp's 32 x 32 bf16 block (64-byte swizzle: 16-byte chunk u
+        // of row r sits at chunk u ^ ((r >> 1) & 3), conflict-free for 8 rows)
+        // and store it with one TMA; rows / columns past the matrix are clipped.
+        float f[32];
+        if (row < p.M) {
+          epilogue_values(p, v, scale, row, col0, f);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = 0.0f;
+        }
+        if (lane == 0) bulk_wait_read<1>();  // the store that used this buffer has read it
+        __syncwarp();
+        const uint32_t buf = smem_u32(sC) + static_cast<uint32_t>((q * 2 + (c & 1)) * C_STAGE_BYTES);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t a = buf + static_cast<uint32_t>(lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4));
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(pack_bf16(f[u * 8 + 0], f[u * 8 + 1])),
+                       "r"(pack_bf16(f[u * 8 + 2], f[u * 8 + 3])), "r"(pack_bf16(f[u * 8 + 4], f[u * 8 + 5])),
+                       "r"(pack_bf16(f[u * 8 + 6], f[u * 8 + 7]))
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, buf, col0, static_cast<int32_t>(row0));
+          bulk_commit();
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -625,6 +671,7 @@ __global__ void __launch_bounds__(256, 1)
     }
   }
 
+  if (warp >= 4 && lane == 0 && p.tma_store) bulk_wait_all();  // staged stores have left shared memory
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // no CTA leaves while its peer may still touch its barriers or shared memory
@@ -656,14 +703,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn(std::string* err) {
 // 64 (cols) x box_rows, 128-byte swizzle, zero fill outside the matrix.
 bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, uint32_t box_rows,
               std::string* err) {
+  return make_map_box(m, base, rows, cols, ld, 64, box_rows, CU_TENSOR_MAP_SWIZZLE_128B, err);
+}
+
+bool make_map_box(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, uint32_t box_cols,
+                  uint32_t box_rows, CUtensorMapSwizzle swizzle, std::string* err) {
   auto fn = encode_fn(err);
   if (!fn) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
-  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     if (err) *err = "cuTensorMapEncodeTiled failed (CUresult " + std::to_string(static_cast<int>(r)) + ")";
@@ -700,8 +752,8 @@ int launch(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int 
   return 0;
 }
 
-int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int pair_tiles, cudaStream_t s,
-                std::string* err) {
+int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                int pair_tiles, cudaStream_t s, std::string* err) {
   static bool attr_set[64] = {};
   static int max_clusters[64] = {};
   int dev = 0;
@@ -753,7 +805,7 @@ int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_pair, ta, tb, kp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_pair, ta, tb, tc, kp);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     if (err) *err = std::string("pair gemm launch: ") + cudaGetErrorString(e);
@@ -768,6 +820,16 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // Kernel choice for TMA-describable operands: the CTA-pair kernel unless
 // TFB200_GEMM_KERNEL=single, or when the problem has too few rows to fill a
 // 256-row pair tile.
+// Stores through shared memory and TMA unless TFB200_GEMM_STORE=direct.
+bool tma_store_enabled() {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* v = std::getenv("TFB200_GEMM_STORE");
+    mode = (v && std::string(v) == "direct") ? 0 : 1;
+  }
+  return mode == 1;
+}
+
 bool use_pair(int64_t M) {
   static int mode = -1;
   if (mode < 0) {
@@ -821,7 +883,10 @@ int run_gemm(const GemmProblem& g, cudaStream_t stream, std::string* err) {
     if (!make_map(&tb, g.B, g.K, g.N, g.ldb, BK, err)) return -3;
     if (use_pair(g.M)) {
       const int pair_tiles = static_cast<int>(((g.M + PBM - 1) / PBM) * ((g.N + BN - 1) / BN));
-      return launch_pair(kp, ta, tb, pair_tiles, stream, err);
+      CUtensorMap tc{};
+      kp.tma_store = aligned16(g.C) && g.ldc % 8 == 0 && tma_store_enabled();
+      if (kp.tma_store && !make_map_box(&tc, g.C, g.M, g.N, g.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B, err)) return -3;
+      return launch_pair(kp, ta, tb, tc, pair_tiles, stream, err);
     }
     return launch<false>(kp, ta, tb, grid, stream, err);
   }

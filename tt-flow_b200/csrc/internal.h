@@ -79,6 +79,8 @@ int launch_residual_add(const float* part, int64_t ldp, const bf16* res, int64_t
 // box of 64 columns x box_rows rows, 128-byte swizzle, zero fill outside.
 bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, uint32_t box_rows,
               std::string* err);
+bool make_map_box(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, uint32_t box_cols,
+                  uint32_t box_rows, CUtensorMapSwizzle swizzle, std::string* err);
 
 // RMSNorm staging pass (rmsnorm_prep.cu): writes bf16(x * gamma) with leading
 // dimension staged_ld(K) and inv[m] = 1/sqrt(mean_k(x^2) + eps) into `ws`
