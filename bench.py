@@ -175,11 +175,23 @@ def cpu_port_tflops(name: str, rows: int, reps: int = 1) -> tuple[float, float, 
     return fl / sec / 1e12, sec, info
 
 
+def _all_host_threads():
+    """torchrun sets OMP_NUM_THREADS=1 for every rank; the CPU legs use all host cores."""
+    try:
+        from threadpoolctl import threadpool_limits
+
+        return threadpool_limits(limits=os.cpu_count() or 1)
+    except Exception:
+        return None
+
+
 def run_reference(args) -> int:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     from tfb200 import workloads as W
+
+    _limits = _all_host_threads()  # noqa: F841 (kept alive for the run)
 
     name = args.workload
     rows = args.ref_rows
@@ -388,6 +400,7 @@ def run_ours(args) -> int:
         "clocks": clocks,
     }
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        _limits = _all_host_threads()  # noqa: F841
         rows = args.cpu_rows
         if rows <= 0:  # size the sample for about 10 s of CPU work
             _, probe, _ = cpu_port_tflops(name, 64)
