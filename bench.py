@@ -256,29 +256,36 @@ def run_ours(args) -> int:
         return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda().view(torch.bfloat16)
 
     tp = wl.kind == "fused_mlp" and d["M"] <= 64
-    if tp:
+    fused_tp = tp and args.tp_reduce == "fused" and world > 1
+    if tp and world > 1:
         # Decode-shaped MLP: tensor parallel over the ranks (W1 by columns, W2 by
-        # rows), one all-reduce of the fp32 partial sum, then the residual add.
-        from tfb200.tp import TPDecodeMLP
+        # rows). "fused": the down-projection kernel reduces across GPUs over
+        # NVLink peer memory and finishes the rows; "nccl": fp32 partial sum, one
+        # NCCL all-reduce, then the residual add.
+        from tfb200.tp import TPDecodeMLP, TPDecodeMLPFused
 
         x, g, w1, b1, w2 = (dev(t[k]) for k in ("x", "gamma", "w1", "b1", "w2"))
-        mlp = TPDecodeMLP(w1, b1, w2, g, rank, world, eps=wl.eps, gelu=wl.gelu)
+        if fused_tp:
+            mlp = TPDecodeMLPFused(w1, b1, w2, g, rank, world, max_rows=d["M"], eps=wl.eps, gelu=wl.gelu)
+        else:
+            mlp = TPDecodeMLP(w1, b1, w2, g, rank, world, eps=wl.eps, gelu=wl.gelu)
         del w1, w2
         torch.cuda.empty_cache()
         y = torch.empty(d["M"], d["N"], dtype=torch.bfloat16, device="cuda")
 
         def step(xin=None):
             xx = x if xin is None else xin
-            mlp(xx, xx, out=y)
+            return mlp(xx, xx) if fused_tp else mlp(xx, xx, out=y)
         in_bytes = x.numel() * 2
     elif wl.kind == "fused_mlp":
+        # One GPU (the decode shape included: the C ABI picks the weight-streaming kernels for few rows).
         x, g, w1, b1, w2 = (dev(t[k]) for k in ("x", "gamma", "w1", "b1", "w2"))
         y = torch.empty(d["M"], d["N"], dtype=torch.bfloat16, device="cuda")
         ws = torch.empty(ops.mlp_workspace_bytes(d["M"], d["K"], d["H"], d["N"]), dtype=torch.uint8, device="cuda")
 
         def step(xin=None):
             xx = x if xin is None else xin
-            ops.fused_mlp(xx, g, w1, b1, w2, xx, wl.eps, gelu=wl.gelu, out=y, workspace=ws)
+            return ops.fused_mlp(xx, g, w1, b1, w2, xx, wl.eps, gelu=wl.gelu, out=y, workspace=ws)
         in_bytes = x.numel() * 2
     elif wl.kind == "fused_rmsnorm_matmul":
         x, g, w = (dev(t[k]) for k in ("x", "gamma", "w"))
@@ -286,14 +293,14 @@ def run_ours(args) -> int:
         ws = torch.empty(ops.rmsnorm_matmul_workspace_bytes(d["M"], d["K"], d["N"]), dtype=torch.uint8, device="cuda")
 
         def step(xin=None):
-            ops.fused_rmsnorm_matmul(x if xin is None else xin, g, w, wl.eps, out=y, workspace=ws)
+            return ops.fused_rmsnorm_matmul(x if xin is None else xin, g, w, wl.eps, out=y, workspace=ws)
         in_bytes = x.numel() * 2
     else:
         x, b = dev(t["a"]), dev(t["b"])
         y = torch.empty(d["M"], d["N"], dtype=torch.bfloat16, device="cuda")
 
         def step(xin=None):
-            ops.matmul(x if xin is None else xin, b, out=y)
+            return ops.matmul(x if xin is None else xin, b, out=y)
         in_bytes = x.numel() * 2
     flops_step = W.flops(name)
 
@@ -338,15 +345,13 @@ def run_ours(args) -> int:
     xd = torch.empty_like(x)
     for _ in range(max(1, args.warmup)):
         xd.copy_(xh, non_blocking=True)
-        step(xd)
-        yh.copy_(y, non_blocking=True)
+        yh.copy_(step(xd), non_blocking=True)
     barrier()
     torch.cuda.synchronize()
     e0.record()
     for _ in range(args.steps):
         xd.copy_(xh, non_blocking=True)
-        step(xd)
-        yh.copy_(y, non_blocking=True)
+        yh.copy_(step(xd), non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
     barrier()
@@ -371,8 +376,13 @@ def run_ours(args) -> int:
                 "peak_source": f"{pk_src} HBM copy bandwidth (MEASURED_PEAKS.json)" if pk_src == "measured"
                 else "fallback"}
         scaling = "strong"
-        parallelism = (f"tensor parallel over {world} GPU(s): W1 by columns, W2 by rows, one NCCL all-reduce"
-                       if world > 1 else "1 GPU, weights whole")
+        if world == 1:
+            parallelism = "1 GPU, weights whole"
+        elif fused_tp:
+            parallelism = (f"tensor parallel over {world} GPUs: W1 by columns, W2 by rows, the reduction fused into "
+                           f"the down-projection kernel over NVLink peer memory")
+        else:
+            parallelism = f"tensor parallel over {world} GPUs: W1 by columns, W2 by rows, one NCCL all-reduce"
     else:
         unit = "TFLOP/s"
         peak = pk["bf16_tflops_sustained"] if sustained else pk["bf16_tflops"]
@@ -413,6 +423,9 @@ def run_ours(args) -> int:
                                           f"restated (numpy/OpenBLAS fp32, libm erf per element)"}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if fused_tp:
+        barrier()
+        mlp.close()
     if world > 1:
         dist.destroy_process_group()
     return 0
@@ -428,6 +441,8 @@ def main() -> int:
     ap.add_argument("--cpu-rows", type=int, default=0, help="rows of the CPU baseline sample (0: about 10 s)")
     ap.add_argument("--ref-rows", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp-reduce", choices=["fused", "nccl"], default="fused",
+                    help="decode workloads: cross-GPU reduction inside the kernel, or an NCCL all-reduce")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

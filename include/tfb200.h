@@ -127,6 +127,46 @@ int tfb200_fused_mlp_partial(const tfb200_mat* x, const void* gamma, const tfb20
                              float* partial, int64_t ld_partial, void* stream, void* workspace,
                              size_t workspace_bytes);
 
+/* Tensor-parallel fused MLP with the all-reduce fused into the down-projection
+ * kernel (NVLink peer memory instead of a separate collective). Column block nb
+ * (128 output columns) is owned by rank nb % world; every rank adds its fp32
+ * partial sums straight into the owner's accumulator (peer atomics), the last
+ * contributor over all ranks adds the residual, rounds to bf16, writes the
+ * block to every rank's output and clears the owner's accumulator; the call
+ * returns (stream-ordered) once every block has reached this rank.
+ * The caller allocates on every rank, zero-filled before the first call, one
+ * buffer of tfb200_tp_buffer_bytes(m, n) and shares it (tfb200_ipc_*), then fills
+ * `comm` with each rank's pointers (tfb200_tp_layout). `epoch` counts the calls
+ * made with these buffers and must be the same on every rank. All ranks must make
+ * the same calls with the same shapes. Waits are bounded (TFB200_ETIMEOUT in the
+ * device status word). Same arguments otherwise as tfb200_fused_mlp_partial plus
+ * the residual; the result is out[rank] (bf16 [M, N], leading dimension N).
+ * No counterpart in the reference, which has no multi-device path. */
+#define TFB200_MAX_TP 8
+typedef struct tfb200_tp_comm {
+  int32_t rank;
+  int32_t world;
+  uint32_t epoch;
+  float* acc[TFB200_MAX_TP];      /* per rank: fp32 [M, N] accumulator */
+  int32_t* counters[TFB200_MAX_TP]; /* per rank: ceil(N/128) arrival counters */
+  void* out[TFB200_MAX_TP];       /* per rank: bf16 [M, N] result */
+  uint32_t* done[TFB200_MAX_TP];  /* per rank: completion counter */
+} tfb200_tp_comm;
+size_t tfb200_tp_buffer_bytes(int64_t m, int64_t n);
+/* Offsets of acc / counters / out / done inside one tfb200_tp_buffer_bytes buffer. */
+int tfb200_tp_layout(int64_t m, int64_t n, size_t* acc_off, size_t* counters_off, size_t* out_off, size_t* done_off);
+int tfb200_fused_mlp_tp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w1_shard, const void* b1_shard,
+                        const tfb200_mat* w2_shard, const tfb200_mat* residual, float eps, int gelu_mode,
+                        const tfb200_tp_comm* comm, void* stream, void* workspace, size_t workspace_bytes);
+
+/* CUDA IPC of a device buffer between the processes of one node:
+ * tfb200_ipc_get writes a 64-byte handle of the allocation holding `ptr` and the
+ * offset of `ptr` in it; tfb200_ipc_open maps a peer's handle and returns the
+ * peer allocation's base (add the offset); tfb200_ipc_close unmaps it. */
+int tfb200_ipc_get(const void* ptr, void* handle64, size_t* offset);
+int tfb200_ipc_open(const void* handle64, void** base);
+int tfb200_ipc_close(void* base);
+
 /* y = bf16(partial + residual): the last step of the tensor-parallel MLP, after
  * the partial sums have been reduced across GPUs (the residual add of
  * golden.py:122). partial is fp32 with leading dimension ld_partial. */

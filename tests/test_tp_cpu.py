@@ -81,3 +81,46 @@ def test_shards_cover_hidden_dimension_once():
     assert np.array_equal(np.concatenate([s.w1 for s in shards], axis=1), c["w1"])
     assert np.array_equal(np.concatenate([s.w2 for s in shards], axis=0), c["w2"])
     assert np.array_equal(np.concatenate([s.b1 for s in shards]), c["b1"])
+
+
+def _exchange_worker(rank, world, port, out_path):
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    sys.path[:0] = [str(root), str(root / "tt-flow_b200")]
+    from tfb200.tp import exchange_handles
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    local = (bytes([rank]) * 64, 256 * rank)
+
+    def gather(obj):
+        out = [None] * world
+        dist.all_gather_object(out, obj)
+        return out
+
+    peers = exchange_handles(local, rank, world, gather)
+    if rank == 0:
+        np.save(out_path, np.array([[h[0], o] for h, o in peers]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ipc_handle_exchange_in_rank_order(tmp_path):
+    """Each rank's IPC handle and offset reach every rank in rank order (gloo stands in for NCCL)."""
+    world = 3
+    port = 30500 + (os.getpid() % 1000)
+    out = str(tmp_path / "peers.npy")
+    mp.start_processes(_exchange_worker, args=(world, port, out), nprocs=world, join=True, start_method="spawn")
+    got = np.load(out)
+    assert got.tolist() == [[r, 256 * r] for r in range(world)]
+
+
+def test_exchange_rejects_misordered_gather():
+    from tfb200.tp import exchange_handles
+
+    with pytest.raises(RuntimeError):
+        exchange_handles((b"a", 0), 0, 2, lambda obj: [(b"b", 0), obj])
+    with pytest.raises(RuntimeError):
+        exchange_handles((b"a", 0), 0, 2, lambda obj: [obj])

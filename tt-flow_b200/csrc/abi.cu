@@ -1,5 +1,7 @@
 // C ABI of libtfb200 (declared in include/tfb200.h): argument validation, error
 // reporting and dispatch to the sm_100a kernels.
+#include <cudaTypedefs.h>
+
 #include <atomic>
 #include <cstring>
 #include <mutex>
@@ -369,6 +371,108 @@ int tfb200_selftest_bounded_wait(uint64_t limit_ns, void* stream) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(TFB200_ECUDA, std::string("selftest launch: ") + cudaGetErrorString(e));
   count_launch();
+  return TFB200_OK;
+}
+
+static size_t al256b(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+
+int tfb200_tp_layout(int64_t m, int64_t n, size_t* acc_off, size_t* counters_off, size_t* out_off, size_t* done_off) {
+  if (m <= 0 || n <= 0) return fail(TFB200_EINVAL, "tfb200_tp_layout: empty shape");
+  const size_t acc = 0;
+  const size_t cnt = acc + al256b(static_cast<size_t>(m) * n * 4);
+  const size_t out = cnt + al256b(static_cast<size_t>((n + 127) / 128) * 4);
+  const size_t done = out + al256b(static_cast<size_t>(m) * n * 2);
+  if (acc_off) *acc_off = acc;
+  if (counters_off) *counters_off = cnt;
+  if (out_off) *out_off = out;
+  if (done_off) *done_off = done;
+  return TFB200_OK;
+}
+
+size_t tfb200_tp_buffer_bytes(int64_t m, int64_t n) {
+  size_t done = 0;
+  if (tfb200_tp_layout(m, n, nullptr, nullptr, nullptr, &done) != TFB200_OK) return 0;
+  return done + 256;
+}
+
+int tfb200_fused_mlp_tp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w1, const void* b1,
+                        const tfb200_mat* w2, const tfb200_mat* residual, float eps, int gelu_mode,
+                        const tfb200_tp_comm* comm, void* stream, void* workspace, size_t workspace_bytes) {
+  std::string err;
+  if (!mat_ok(x, "x", &err) || !mat_ok(w1, "w1", &err) || !mat_ok(w2, "w2", &err) ||
+      !mat_ok(residual, "residual", &err))
+    return fail(TFB200_EINVAL, "tfb200_fused_mlp_tp: " + err);
+  if (!comm || comm->world < 1 || comm->world > TFB200_MAX_TP || comm->rank < 0 || comm->rank >= comm->world)
+    return fail(TFB200_EINVAL, "tfb200_fused_mlp_tp: bad communicator (rank / world)");
+  const int64_t M = x->rows, K = x->cols, H = w1->cols, N = w2->cols;
+  if (w1->rows != K || w2->rows != H || residual->rows != M || residual->cols != N)
+    return fail(TFB200_EINVAL, "tfb200_fused_mlp_tp: shapes do not chain (X[M,K], W1[K,H], W2[H,N], R[M,N])");
+  if (gelu_mode != TFB200_GELU_ERF && gelu_mode != TFB200_GELU_TANH)
+    return fail(TFB200_EINVAL, "tfb200_fused_mlp_tp: bad gelu_mode");
+  if (!(eps >= 0.0f) || !gamma || K == 0) return fail(TFB200_EINVAL, "tfb200_fused_mlp_tp: bad eps / gamma / K");
+  if (M == 0 || N == 0) return TFB200_OK;
+  for (int r = 0; r < comm->world; ++r)
+    if (!comm->acc[r] || !comm->counters[r] || !comm->out[r] || !comm->done[r])
+      return fail(TFB200_EINVAL, "tfb200_fused_mlp_tp: missing peer buffer");
+  if (!decode_eligible(M, w1->data, w1->ld, w2->data, w2->ld) || H % 8 != 0)
+    return fail(TFB200_EUNSUPPORTED,
+                "tfb200_fused_mlp_tp: needs M <= 64, 16-byte aligned weights with ld % 8 == 0, H % 8 == 0");
+  const size_t need = tfb200_fused_mlp_partial_workspace_size(M, K, H, N);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(TFB200_EWORKSPACE, "tfb200_fused_mlp_tp: workspace missing, small or not 256-byte aligned");
+  TpPeers tp;
+  tp.rank = comm->rank;
+  tp.world = comm->world;
+  tp.epoch = comm->epoch;
+  for (int r = 0; r < comm->world; ++r) {
+    tp.acc[r] = comm->acc[r];
+    tp.cnt[r] = comm->counters[r];
+    tp.out[r] = static_cast<bf16*>(comm->out[r]);
+    tp.done[r] = comm->done[r];
+  }
+  const int rc = run_decode_mlp(as_bf16(x->data), x->ld, as_bf16(gamma), as_bf16(w1->data), w1->ld, as_bf16(b1),
+                                as_bf16(w2->data), w2->ld, as_bf16(residual->data), residual->ld, eps,
+                                gelu_mode == TFB200_GELU_ERF ? kGeluErf : kGeluTanh, nullptr, 0, nullptr, 0, M, K, H,
+                                N, workspace, static_cast<cudaStream_t>(stream), &err, &tp);
+  return rc ? fail(rc, "tfb200_fused_mlp_tp: " + err) : TFB200_OK;
+}
+
+int tfb200_ipc_get(const void* ptr, void* handle64, size_t* offset) {
+  if (!ptr || !handle64) return fail(TFB200_EINVAL, "tfb200_ipc_get: null argument");
+  static PFN_cuMemGetAddressRange_v3020 range_fn = nullptr;
+  if (!range_fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return fail(TFB200_ECUDA, "tfb200_ipc_get: cuMemGetAddressRange unavailable");
+    range_fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(f);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(TFB200_ECUDA, "tfb200_ipc_get: pointer is not a device allocation");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return fail(TFB200_ECUDA, std::string("cudaIpcGetMemHandle: ") + cudaGetErrorString(e));
+  static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t is 64 bytes");
+  std::memcpy(handle64, &h, sizeof(h));
+  if (offset) *offset = static_cast<size_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return TFB200_OK;
+}
+
+int tfb200_ipc_open(const void* handle64, void** base) {
+  if (!handle64 || !base) return fail(TFB200_EINVAL, "tfb200_ipc_open: null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(TFB200_ECUDA, std::string("cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+  return TFB200_OK;
+}
+
+int tfb200_ipc_close(void* base) {
+  const cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return fail(TFB200_ECUDA, std::string("cudaIpcCloseMemHandle: ") + cudaGetErrorString(e));
   return TFB200_OK;
 }
 

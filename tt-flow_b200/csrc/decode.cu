@@ -54,7 +54,7 @@ bool decode_eligible(int64_t m, const void* w1, int64_t ldw1, const void* w2, in
 int run_decode_mlp(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* w1, int64_t ldw1, const bf16* b1,
                    const bf16* w2, int64_t ldw2, const bf16* residual, int64_t ldr, float eps, int gelu, bf16* y,
                    int64_t ldy, float* out_partial, int64_t ldp, int64_t M, int64_t K, int64_t H, int64_t N,
-                   void* ws, cudaStream_t s, std::string* err) {
+                   void* ws, cudaStream_t s, std::string* err, const TpPeers* tp) {
   char* base = static_cast<char*>(ws);
   bf16* hid = reinterpret_cast<bf16*>(base);
   base += al256(static_cast<size_t>(M) * H * 2);
@@ -74,8 +74,8 @@ int run_decode_mlp(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* w1
   // padding between rows is cleared separately.
   const size_t clear_bytes = static_cast<size_t>(reinterpret_cast<char*>(cnt2) - reinterpret_cast<char*>(acc1)) +
                              al256(stream_counter_bytes(N)) +
-                             (out_partial ? 0 : al256(static_cast<size_t>(M) * N * 4));
-  if (out_partial) {
+                             ((out_partial || tp) ? 0 : al256(static_cast<size_t>(M) * N * 4));
+  if (out_partial && !tp) {
     const cudaError_t e = ld2 == N ? cudaMemsetAsync(acc2, 0, static_cast<size_t>(M) * N * 4, s)
                                    : cudaMemset2DAsync(acc2, ld2 * 4, 0, N * 4, M, s);
     if (e != cudaSuccess) {
@@ -120,7 +120,15 @@ int run_decode_mlp(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* w1
   dn.ldw = ldw2;
   dn.acc = acc2;
   dn.counters = cnt2;
-  if (out_partial) {
+  if (tp) {
+    // Down-projection and the cross-GPU reduction in one kernel; the peers'
+    // accumulators clean themselves, so nothing to clear here.
+    dn.mode = kStreamTpReduce;
+    dn.tp = *tp;
+    dn.residual = residual;
+    dn.ldr = ldr;
+    dn.ldo = N;
+  } else if (out_partial) {
     dn.mode = kStreamPartial;
   } else {
     dn.mode = kStreamFinishDown;
@@ -132,7 +140,7 @@ int run_decode_mlp(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* w1
   // The counters and the fp32 accumulator of this pass must not be the ones the
   // up pass used: they are separate regions of the workspace (or the caller's
   // partial buffer).
-  if (dn.mode != kStreamPartial && ld2 != N) {
+  if (dn.mode == kStreamFinishDown && ld2 != N) {
     *err = "decode MLP: internal accumulator layout";
     return -3;
   }

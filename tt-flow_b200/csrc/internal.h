@@ -41,7 +41,22 @@ int run_gemm(const GemmProblem& p, cudaStream_t stream, std::string* err);
 
 // Weight-streaming GEMM for few rows (stream_sm100.cu): acc[M,N] (+)= A[M,K] @ W[K,N]
 // split over all SMs, then a per-column-block finishing epilogue.
-enum StreamMode : int { kStreamPartial = 0, kStreamFinishUp = 1, kStreamFinishDown = 2 };
+enum StreamMode : int { kStreamPartial = 0, kStreamFinishUp = 1, kStreamFinishDown = 2, kStreamTpReduce = 3 };
+constexpr int kMaxTp = 8;
+// Peer buffers of the tensor-parallel reduction fused into the down-projection
+// (kStreamTpReduce). Column block nb of the output is owned by rank nb % world:
+// every rank adds its fp32 partial into the owner's accumulator over NVLink, the
+// last contributor (across all ranks) adds the residual, rounds, writes the block
+// to every rank's output, clears the owner's accumulator and bumps every rank's
+// done counter. Counters are monotonic: `epoch` numbers the calls.
+struct TpPeers {
+  int rank = 0, world = 1;
+  uint32_t epoch = 0;
+  float* acc[kMaxTp] = {};
+  int* cnt[kMaxTp] = {};
+  bf16* out[kMaxTp] = {};
+  unsigned int* done[kMaxTp] = {};
+};
 struct StreamProblem {
   int64_t M = 0, N = 0, K = 0;
   const bf16* A = nullptr;  // [M, K] tokens
@@ -58,6 +73,7 @@ struct StreamProblem {
   int64_t ldr = 0;
   bf16* out = nullptr;
   int64_t ldo = 0;
+  TpPeers tp;  // kStreamTpReduce
 };
 int run_stream(const StreamProblem& p, cudaStream_t stream, std::string* err);
 int stream_mpad(int64_t m);
@@ -71,7 +87,7 @@ bool decode_eligible(int64_t m, const void* w1, int64_t ldw1, const void* w2, in
 int run_decode_mlp(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* w1, int64_t ldw1, const bf16* b1,
                    const bf16* w2, int64_t ldw2, const bf16* residual, int64_t ldr, float eps, int gelu, bf16* y,
                    int64_t ldy, float* out_partial, int64_t ldp, int64_t M, int64_t K, int64_t H, int64_t N,
-                   void* ws, cudaStream_t s, std::string* err);
+                   void* ws, cudaStream_t s, std::string* err, const TpPeers* tp = nullptr);
 int launch_residual_add(const float* part, int64_t ldp, const bf16* res, int64_t ldr, bf16* y, int64_t ldy,
                         int64_t M, int64_t N, cudaStream_t s, std::string* err);
 

@@ -56,6 +56,7 @@ struct SParams {
   uint32_t tmem_cols;
   int* status;
   uint64_t timeout_ns;
+  TpPeers tp;
 };
 
 struct SCtl {
@@ -112,6 +113,52 @@ __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + e
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
   return 0.5f * x * (1.0f + tanh_approx(u));
+}
+
+// Cross-GPU arrival on column block nb and, for the last contributor over all
+// ranks, the finish: residual, bf16, store to every rank, clear the owner's
+// accumulator, bump every rank's done counter. Called by the 128 epilogue threads.
+__device__ __forceinline__ void tp_arrive_and_finish(const SParams& p, SCtl* ctl, int nb, int et, int G) {
+  const int owner = nb % p.tp.world;
+  __threadfence_system();  // this CTA's atomics on the owner's accumulator come first
+  epi_bar();
+  if (et == 0) {
+    const int64_t first_u = static_cast<int64_t>(nb) * p.kblocks;
+    const unsigned per_rank =
+        static_cast<unsigned>(cta_of(first_u + p.kblocks - 1, p.units, G) - cta_of(first_u, p.units, G) + 1);
+    const unsigned total = per_rank * static_cast<unsigned>(p.tp.world);
+    const unsigned prev = atomicAdd_system(reinterpret_cast<unsigned*>(p.tp.cnt[owner]) + nb, 1u);
+    ctl->finisher = (prev + 1u == (p.tp.epoch + 1u) * total);
+  }
+  epi_bar();
+  if (!ctl->finisher) return;
+  __threadfence_system();
+  float* accp = p.tp.acc[owner];
+  const int nf = nb * SBN + et;
+  if (nf < p.N) {
+    for (int m0 = 0; m0 < p.M; m0 += 8) {
+      float val[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int m = m0 + j;
+        val[j] = m < p.M ? __ldcv(accp + static_cast<int64_t>(m) * p.N + nf) +
+                               __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ldr + nf])
+                         : 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int m = m0 + j;
+        if (m >= p.M) break;
+        const bf16 o = __float2bfloat16_rn(val[j]);
+        for (int r = 0; r < p.tp.world; ++r) p.tp.out[r][static_cast<int64_t>(m) * p.ldo + nf] = o;
+        accp[static_cast<int64_t>(m) * p.N + nf] = 0.0f;  // ready for the next call
+      }
+    }
+  }
+  __threadfence_system();
+  epi_bar();
+  if (et == 0)
+    for (int r = 0; r < p.tp.world; ++r) atomicAdd_system(p.tp.done[r], 1u);
 }
 
 __global__ void __launch_bounds__(256, 1)
@@ -262,16 +309,23 @@ __global__ void __launch_bounds__(256, 1)
                        v);
         tmem_wait_ld();
         if (n < p.N) {
+          // Tensor-parallel reduction: the partial goes straight into the owning
+          // rank's accumulator (an NVLink peer address unless this rank owns it).
+          float* dst = p.mode == kStreamTpReduce ? p.tp.acc[nb % p.tp.world] : p.acc;
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int m = c0 + j;
-            if (m < p.M) atomicAdd(p.acc + static_cast<int64_t>(m) * p.N + n, __uint_as_float(v[j]));
+            if (m < p.M) atomicAdd(dst + static_cast<int64_t>(m) * p.N + n, __uint_as_float(v[j]));
           }
         }
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl->tempty[acc]));
       if (p.mode == kStreamPartial) continue;
+      if (p.mode == kStreamTpReduce) {
+        tp_arrive_and_finish(p, ctl, nb, et, G);
+        continue;
+      }
       // Arrive on the column block's counter; the last contributor finishes it.
       __threadfence();
       epi_bar();
@@ -319,6 +373,20 @@ __global__ void __launch_bounds__(256, 1)
     }
   }
 
+  // Tensor-parallel: the call is complete on this rank once every column block
+  // (finished on whichever rank) has landed here. One thread waits, bounded.
+  if (p.mode == kStreamTpReduce && blockIdx.x == 0 && threadIdx.x == 0) {
+    const unsigned target = (p.tp.epoch + 1u) * static_cast<unsigned>(p.nblocks);
+    const volatile unsigned* done = p.tp.done[p.tp.rank];
+    const uint64_t t0 = global_ns();
+    while (static_cast<int>(*done - target) < 0) {
+      if (global_ns() - t0 > p.timeout_ns) {
+        atomicExch(p.status, kDevTimeout);
+        break;
+      }
+    }
+    __threadfence_system();
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
@@ -363,6 +431,12 @@ int run_stream(const StreamProblem& sp, cudaStream_t stream, std::string* err) {
   p.ldr = sp.ldr;
   p.out = sp.out;
   p.ldo = sp.ldo;
+  p.tp = sp.tp;
+  if (sp.mode == kStreamTpReduce && (sp.tp.world < 1 || sp.tp.world > kMaxTp || sp.tp.rank < 0 ||
+                                     sp.tp.rank >= sp.tp.world)) {
+    if (err) *err = "weight-streaming GEMM: bad tensor-parallel rank / world";
+    return -1;
+  }
   p.status = status;
   p.timeout_ns = wait_limit_ns();
   const uint32_t a_stage = static_cast<uint32_t>(p.Mpad) * SBK * 2;

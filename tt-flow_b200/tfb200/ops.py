@@ -24,7 +24,8 @@ import torch
 
 from . import _lib as L
 
-__all__ = ["matmul", "fused_rmsnorm_matmul", "fused_mlp", "fused_mlp_partial", "residual_add", "mlp_workspace_bytes",
+__all__ = ["matmul", "fused_rmsnorm_matmul", "fused_mlp", "fused_mlp_partial", "fused_mlp_tp", "residual_add",
+           "mlp_workspace_bytes",
            "rmsnorm_matmul_workspace_bytes", "mat", "stream_ptr"]
 
 
@@ -169,6 +170,34 @@ def fused_mlp_partial(x: torch.Tensor, gamma: torch.Tensor, w1_shard: torch.Tens
         ctypes.c_int(_GELU[gelu]), ctypes.c_void_p(y.data_ptr()), ctypes.c_int64(y.stride(0)),
         ctypes.c_void_p(stream_ptr()), ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel())))
     return y
+
+
+def fused_mlp_tp(x: torch.Tensor, gamma: torch.Tensor, w1_shard: torch.Tensor, b1_shard: torch.Tensor | None,
+                 w2_shard: torch.Tensor, residual: torch.Tensor, comm: L.TpComm, eps: float = 1e-6,
+                 gelu: str = "erf", workspace: torch.Tensor | None = None) -> None:
+    """One rank's call of the tensor-parallel MLP whose all-reduce is fused into the down-projection kernel
+    (``tfb200_fused_mlp_tp``). The result lands in every rank's ``comm.out`` buffer; ``tp.TPDecodeMLPFused``
+    owns the buffers and the epoch."""
+    x2 = _rows2d(x, "x")
+    W1 = _rows2d(w1_shard, "w1_shard")
+    W2 = _rows2d(w2_shard, "w2_shard")
+    r2 = _rows2d(residual, "residual")
+    M, K = x2.shape
+    H, N = W1.shape[1], W2.shape[1]
+    if W1.shape[0] != K or W2.shape[0] != H:
+        raise ValueError("fused_mlp_tp: shapes do not chain")
+    if tuple(r2.shape) != (M, N):
+        raise ValueError(f"fused_mlp_tp: residual must be [{M},{N}] (got {tuple(r2.shape)})")
+    if gelu not in _GELU:
+        raise ValueError(f"gelu must be 'erf' or 'tanh' (got {gelu!r})")
+    b = _vec(b1_shard, H, "b1_shard")
+    g = _vec(gamma, K, "gamma")
+    ws = _workspace(int(L.lib().tfb200_fused_mlp_partial_workspace_size(M, K, H, N)), workspace, x.device)
+    L.check(L.lib().tfb200_fused_mlp_tp(
+        ctypes.byref(mat(x2)), ctypes.c_void_p(g.data_ptr()), ctypes.byref(mat(W1)),
+        ctypes.c_void_p(b.data_ptr() if b is not None else None), ctypes.byref(mat(W2)), ctypes.byref(mat(r2)),
+        ctypes.c_float(eps), ctypes.c_int(_GELU[gelu]), ctypes.byref(comm), ctypes.c_void_p(stream_ptr()),
+        ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel())))
 
 
 def residual_add(partial: torch.Tensor, residual: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -9,6 +9,11 @@ sum), one all-reduce sums the partials (NCCL over NVLink / NVSwitch through
 ``torch.distributed``), and ``ops.residual_add`` adds the residual and rounds.
 RMSNorm is computed redundantly on every GPU from the full X.
 
+``TPDecodeMLPFused`` drops the separate all-reduce: the down-projection kernel
+adds its fp32 partial sums straight into the owning rank's accumulator over
+NVLink peer memory (CUDA IPC between the processes), and the last contributor to
+each 128-column block finishes it (residual, bf16) and writes it to every rank.
+
 The host logic takes its partial, all-reduce and finish steps as arguments so
 that the sharding and reduction order can be checked on CPU ranks (gloo).
 """
@@ -18,7 +23,7 @@ from __future__ import annotations
 from dataclasses import dataclass
 from typing import Callable
 
-__all__ = ["Shard", "shard_mlp", "tp_forward", "TPDecodeMLP"]
+__all__ = ["Shard", "shard_mlp", "tp_forward", "TPDecodeMLP", "TPDecodeMLPFused", "exchange_handles"]
 
 
 @dataclass
@@ -91,3 +96,106 @@ class TPDecodeMLP:
     def __call__(self, x, residual, out=None):
         return tp_forward(x, residual, self.shard, self.partial, self.all_reduce,
                           lambda p, r: self.ops.residual_add(p, r, out=out))
+
+
+def exchange_handles(local: tuple, rank: int, world: int, gather_fn: Callable) -> list:
+    """Every rank's (handle bytes, offset) pair, in rank order. ``gather_fn(obj)`` returns the list of
+    all ranks' objects (``torch.distributed.all_gather_object`` on GPUs, a gloo group on CPU)."""
+    got = gather_fn(local)
+    if len(got) != world:
+        raise RuntimeError(f"handle exchange returned {len(got)} entries for {world} ranks")
+    if tuple(got[rank]) != tuple(local):
+        raise RuntimeError("handle exchange returned another rank's entry in this rank's slot")
+    return [tuple(g) for g in got]
+
+
+class TPDecodeMLPFused:
+    """The decode MLP on `world` GPUs with the all-reduce inside the down-projection kernel.
+
+    Every rank allocates one zero-filled buffer (fp32 accumulator, column-block counters, bf16 output, done
+    counter) for up to ``max_rows`` token rows, shares it with CUDA IPC and keeps a call counter (the epoch)
+    that must advance in step on every rank. ``__call__`` returns a view of this rank's output buffer, valid
+    until the next call. After a device timeout the buffers are in an unknown state: build a new instance.
+    """
+
+    def __init__(self, w1, b1, w2, gamma, rank: int, world: int, max_rows: int = 64, eps: float = 1e-5,
+                 gelu: str = "tanh", group=None):
+        import ctypes
+
+        import torch
+
+        from . import _lib as L
+        from . import ops
+
+        if not 1 <= world <= L.MAX_TP:
+            raise ValueError(f"world size {world} outside 1..{L.MAX_TP}")
+        self.L, self.ops, self.torch, self.ctypes = L, ops, torch, ctypes
+        self.shard = shard_mlp(w1, b1, w2, rank, world)
+        self.gamma, self.eps, self.gelu = gamma, eps, gelu
+        self.rank, self.world, self.max_rows = rank, world, max_rows
+        self.N = w2.shape[1]
+        lib = L.lib()
+        nbytes = int(lib.tfb200_tp_buffer_bytes(max_rows, self.N))
+        if nbytes == 0:
+            raise ValueError("tfb200_tp_buffer_bytes: bad shape")
+        offs = [ctypes.c_size_t() for _ in range(4)]
+        L.check(lib.tfb200_tp_layout(max_rows, self.N, *[ctypes.byref(o) for o in offs]))
+        self.offsets = [o.value for o in offs]
+        self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=w1.device)
+        torch.cuda.synchronize(w1.device)
+        self._opened = []
+        bases = [0] * world
+        if world > 1:
+            import torch.distributed as dist
+
+            handle = (ctypes.c_char * 64)()
+            off = ctypes.c_size_t()
+            L.check(lib.tfb200_ipc_get(ctypes.c_void_p(self.buf.data_ptr()), handle, ctypes.byref(off)))
+
+            def gather(obj):
+                out = [None] * world
+                dist.all_gather_object(out, obj, group=group)
+                return out
+
+            peers = exchange_handles((bytes(handle), off.value), rank, world, gather)
+            for r, (h, o) in enumerate(peers):
+                if r == rank:
+                    bases[r] = self.buf.data_ptr()
+                    continue
+                base = ctypes.c_void_p()
+                L.check(lib.tfb200_ipc_open(ctypes.create_string_buffer(h, 64), ctypes.byref(base)))
+                self._opened.append(base.value)
+                bases[r] = base.value + o
+        else:
+            bases[0] = self.buf.data_ptr()
+        self.comm = L.TpComm()
+        self.comm.rank, self.comm.world, self.comm.epoch = rank, world, 0
+        a, c, o, d = self.offsets
+        for r in range(world):
+            self.comm.acc[r] = bases[r] + a
+            self.comm.counters[r] = bases[r] + c
+            self.comm.out[r] = bases[r] + o
+            self.comm.done[r] = bases[r] + d
+        self._out_flat = self.buf[o:o + max_rows * self.N * 2].view(torch.bfloat16)
+        self._ws = None
+        # Every rank's buffer is zero before any rank's first call.
+        if world > 1:
+            torch.distributed.barrier(group=group)
+
+    def __call__(self, x, residual):
+        M = x.reshape(-1, x.shape[-1]).shape[0]
+        if M > self.max_rows:
+            raise ValueError(f"{M} token rows, this instance was built for at most {self.max_rows}")
+        if self._ws is None:
+            K, H = self.shard.w1.shape
+            need = int(self.L.lib().tfb200_fused_mlp_partial_workspace_size(self.max_rows, K, H, self.N))
+            self._ws = self.torch.empty(max(need, 256), dtype=self.torch.uint8, device=x.device)
+        self.ops.fused_mlp_tp(x, self.gamma, self.shard.w1, self.shard.b1, self.shard.w2, residual, self.comm,
+                              self.eps, self.gelu, workspace=self._ws)
+        self.comm.epoch = (self.comm.epoch + 1) & 0xFFFFFFFF
+        return self._out_flat[:M * self.N].view(M, self.N)
+
+    def close(self):
+        for base in self._opened:
+            self.L.lib().tfb200_ipc_close(self.ctypes.c_void_p(base))
+        self._opened = []
