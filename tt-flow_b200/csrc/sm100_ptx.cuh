@@ -76,6 +76,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const v
 
 // ----------------------------------------------------------------------- TMA
 
+// Programmatic dependent launch: wait for the preceding grid (complete, its
+// writes visible) / let the next grid in the stream start its prologue.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// fp32 load with system-scope relaxed semantics (another GPU may have written it).
+__device__ __forceinline__ float ld_relaxed_sys(const float* ptr) {
+  float v;
+  asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }

@@ -1,7 +1,7 @@
 // Weight-streaming (decode-shaped) GEMM for sm_100a: few token rows, large
 // weights. HBM-bound: the job is to stream W at full bandwidth from every SM.
 //
-// Computes acc[M, N] = A[M, K] @ W[K, N] with M <= 256 (tokens) through the
+// Computes acc[M, N] = A[M, K] @ W[K, N] with M <= 64 (tokens) through the
 // transposed product acc^T = W^T A^T ("swap AB"): the MMA's M side is 128 output
 // features (W columns, read N-major straight from row-major W) and its N side is
 // the token count rounded up to 32, so no MMA row is wasted on padding tokens.
@@ -15,8 +15,12 @@
 //   mode kFinishDown: out = bf16(acc + residual[m, n])
 //   mode kPartial:    nothing (acc is the result, e.g. a tensor-parallel partial
 //                     sum reduced across GPUs afterwards)
+//   mode kTpReduce:   the partial goes into the owning GPU's accumulator over
+//                     NVLink; the last contributor across GPUs adds the residual
+//                     and writes the block to every GPU (TpPeers).
 // `acc` and the counters must be zero on entry (the RMSNorm staging pass clears
-// them).
+// them). Launched with programmatic stream serialization: the prologue and the
+// first ring of weight tiles overlap the preceding grid's tail.
 //
 // Warp roles: warp 0 TMA producer (W tile 64k x 128n as two 64-column boxes,
 // A tile Mpad x 64k), warp 1 MMA issuer (tcgen05.mma 128 x Mpad x 16, two TMEM
@@ -26,6 +30,8 @@
 // This is the small-M form of the MLP compute the reference emits
 // (tensixflow lib/tensixflow/Codegen/EmitCompute.cpp:331-558).
 #include <cudaTypedefs.h>
+
+#include <cstdlib>
 
 #include "internal.h"
 #include "sm100_ptx.cuh"
@@ -78,6 +84,29 @@ __device__ __forceinline__ int cta_of(int64_t u, int units, int grid) {
   return static_cast<int>(((u + 1) * grid + units - 1) / units - 1);
 }
 
+// A CTA's unit range [u0, u1) cut at column-block boundaries gives its
+// segments, one TMEM accumulation and epilogue each, taken in order. (Taking
+// the column blocks a CTA covers whole first measured 1-3 us slower.)
+struct Segs {
+  int64_t u0, u1;
+  int kb;
+  int first_blk, n;  // column blocks touched
+};
+__device__ __forceinline__ Segs make_segs(int64_t u0, int64_t u1, int kb) {
+  Segs g;
+  g.u0 = u0;
+  g.u1 = u1;
+  g.kb = kb;
+  g.first_blk = u1 > u0 ? static_cast<int>(u0 / kb) : 0;
+  g.n = u1 > u0 ? static_cast<int>((u1 - 1) / kb) - g.first_blk + 1 : 0;
+  return g;
+}
+__device__ __forceinline__ void seg_range(const Segs& g, int i, int64_t* s, int64_t* e, int* nb) {
+  *nb = g.first_blk + i;
+  *s = max(g.u0, static_cast<int64_t>(*nb) * g.kb);
+  *e = min(g.u1, static_cast<int64_t>(*nb + 1) * g.kb);
+}
+
 __device__ __forceinline__ void raise_abort(SCtl* ctl, int* status) {
   ctl->abort = 1;
   atomicExch(status, kDevTimeout);
@@ -115,50 +144,96 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + tanh_approx(u));
 }
 
+// The residual column a finishing thread needs, read into registers (bf16
+// pairs) when its segment starts, before the accumulator is ready: read at
+// finishing time these loads miss L2 (the weight stream has evicted the
+// residual) and cost more than the rest of the finish.
+constexpr int kResRegs = static_cast<int>(kStreamMaxRows / 2);
+__device__ __forceinline__ void load_residual(const SParams& p, int nf, uint32_t (&res)[kResRegs]) {
+  const unsigned short* r = reinterpret_cast<const unsigned short*>(p.residual);
+#pragma unroll
+  for (int i = 0; i < kResRegs; ++i) {
+    const int m = 2 * i;
+    const uint32_t lo = m < p.M ? r[static_cast<int64_t>(m) * p.ldr + nf] : 0u;
+    const uint32_t hi = m + 1 < p.M ? r[static_cast<int64_t>(m + 1) * p.ldr + nf] : 0u;
+    res[i] = lo | (hi << 16);
+  }
+}
+__device__ __forceinline__ float residual_at(const uint32_t (&res)[kResRegs], int m) {
+  return __uint_as_float((m & 1) ? (res[m >> 1] & 0xFFFF0000u) : (res[m >> 1] << 16));
+}
+
+// Element i of a per-rank pointer array in the kernel parameters, read with
+// constant indices only: a runtime index into a parameter array makes the
+// compiler go through a local copy on every access.
+template <typename T>
+__device__ __forceinline__ T* tp_pick(T* const (&arr)[kMaxTp], int i) {
+  T* r = arr[0];
+#pragma unroll
+  for (int k = 1; k < kMaxTp; ++k)
+    if (i == k) r = arr[k];
+  return r;
+}
+
 // Cross-GPU arrival on column block nb and, for the last contributor over all
 // ranks, the finish: residual, bf16, store to every rank, clear the owner's
-// accumulator, bump every rank's done counter. Called by the 128 epilogue threads.
-__device__ __forceinline__ void tp_arrive_and_finish(const SParams& p, SCtl* ctl, int nb, int et, int G) {
+// accumulator, bump every rank's done counter. Called by the 128 epilogue
+// threads after their atomics on the owner's accumulator. One thread orders
+// the block's memory operations at system scope (a fence after the barrier
+// covers what the other threads did before it).
+__device__ __forceinline__ void tp_arrive_and_finish(const SParams& p, SCtl* ctl, int nb, int et, int G,
+                                                     const uint32_t (&res)[kResRegs]) {
   const int owner = nb % p.tp.world;
-  __threadfence_system();  // this CTA's atomics on the owner's accumulator come first
   epi_bar();
   if (et == 0) {
     const int64_t first_u = static_cast<int64_t>(nb) * p.kblocks;
     const unsigned per_rank =
         static_cast<unsigned>(cta_of(first_u + p.kblocks - 1, p.units, G) - cta_of(first_u, p.units, G) + 1);
     const unsigned total = per_rank * static_cast<unsigned>(p.tp.world);
-    const unsigned prev = atomicAdd_system(reinterpret_cast<unsigned*>(p.tp.cnt[owner]) + nb, 1u);
-    ctl->finisher = (prev + 1u == (p.tp.epoch + 1u) * total);
+    __threadfence_system();  // the block's partial sums before its arrival
+    const unsigned prev = atomicAdd_system(reinterpret_cast<unsigned*>(tp_pick(p.tp.cnt, owner)) + nb, 1u);
+    const bool fin = prev + 1u == (p.tp.epoch + 1u) * total;
+    if (fin) __threadfence_system();  // every rank's partial sums before the reads
+    ctl->finisher = fin;
   }
   epi_bar();
   if (!ctl->finisher) return;
-  __threadfence_system();
-  float* accp = p.tp.acc[owner];
+  float* accp = tp_pick(p.tp.acc, owner);
+  bf16* outs[kMaxTp];
+#pragma unroll
+  for (int r = 0; r < kMaxTp; ++r) outs[r] = r < p.tp.world ? p.tp.out[r] : nullptr;
   const int nf = nb * SBN + et;
   if (nf < p.N) {
-    for (int m0 = 0; m0 < p.M; m0 += 8) {
-      float val[8];
+    // Sixteen rows per step: the accumulator may be a peer's, one NVLink round
+    // trip per step.
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+    for (int m0 = 0; m0 < kStreamMaxRows; m0 += 16) {
+      if (m0 >= p.M) break;
+      float val[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
         const int m = m0 + j;
-        val[j] = m < p.M ? __ldcv(accp + static_cast<int64_t>(m) * p.N + nf) +
-                               __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ldr + nf])
-                         : 0.0f;
+        val[j] = m < p.M ? ld_relaxed_sys(accp + static_cast<int64_t>(m) * p.N + nf) : 0.0f;
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 16; ++j) {
         const int m = m0 + j;
         if (m >= p.M) break;
-        const bf16 o = __float2bfloat16_rn(val[j]);
-        for (int r = 0; r < p.tp.world; ++r) p.tp.out[r][static_cast<int64_t>(m) * p.ldo + nf] = o;
+        const bf16 o = __float2bfloat16_rn(val[j] + residual_at(res, m));
+#pragma unroll
+        for (int r = 0; r < kMaxTp; ++r)
+          if (r < p.tp.world) outs[r][static_cast<int64_t>(m) * p.ldo + nf] = o;
         accp[static_cast<int64_t>(m) * p.N + nf] = 0.0f;  // ready for the next call
       }
     }
   }
-  __threadfence_system();
   epi_bar();
-  if (et == 0)
-    for (int r = 0; r < p.tp.world; ++r) atomicAdd_system(p.tp.done[r], 1u);
+  if (et == 0) {
+    __threadfence_system();  // the block's rows on every rank before the done counts
+#pragma unroll
+    for (int r = 0; r < kMaxTp; ++r)
+      if (r < p.tp.world) atomicAdd_system(p.tp.done[r], 1u);
+  }
 }
 
 __global__ void __launch_bounds__(256, 1)
@@ -201,31 +276,61 @@ __global__ void __launch_bounds__(256, 1)
   const int64_t u0 = unit_start(blockIdx.x, p.units, G);
   const int64_t u1 = unit_start(blockIdx.x + 1, p.units, G);
 
+  const Segs segs = make_segs(u0, u1, p.kblocks);
+  // The next grid in the stream (launched with programmatic serialization) may
+  // start its prologue as soon as SMs free up; it still waits for this grid to
+  // complete before it reads anything this grid writes.
+  grid_dep_launch();
+
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       uint32_t armed = 0, armed_phase = 0;
       bool ok = true;
-      for (int64_t u = u0; u < u1; ++u) {
-        const int nb = static_cast<int>(u / p.kblocks);
-        const int kb = static_cast<int>(u % p.kblocks);
-        if (!mbar_wait(smem_u32(&ctl->empty[stage]), phase ^ 1u, &ctl->abort, p.timeout_ns)) {
-          raise_abort(ctl, p.status);
-          ok = false;
-          break;
+      // The first ring of weight tiles is requested before waiting for the
+      // preceding grid (the RMSNorm staging or the up-projection, which never
+      // write the weights); their token tiles follow once it has completed.
+      bool waited = false;
+      int pre = 0;
+      int pre_kb[kMaxStages];
+      for (int si = 0; si < segs.n && ok; ++si) {
+        int64_t s0, e0;
+        int nb;
+        seg_range(segs, si, &s0, &e0, &nb);
+        for (int64_t u = s0; u < e0; ++u) {
+          const int kb = static_cast<int>(u - static_cast<int64_t>(nb) * p.kblocks);
+          if (!waited && pre == p.stages) {
+            grid_dep_wait();
+            for (int i = 0; i < pre; ++i)
+              tma_load_2d(smem_u32(sA + i * a_stage), &tmA, smem_u32(&ctl->full[i]), pre_kb[i] * SBK, 0);
+            waited = true;
+          }
+          if (!mbar_wait(smem_u32(&ctl->empty[stage]), phase ^ 1u, &ctl->abort, p.timeout_ns)) {
+            raise_abort(ctl, p.status);
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&ctl->full[stage]);
+          mbar_arrive_expect_tx(fb, W_STAGE + a_stage);
+          tma_load_2d(smem_u32(sW + stage * W_STAGE), &tmW, fb, nb * SBN, kb * SBK);
+          tma_load_2d(smem_u32(sW + stage * W_STAGE + 8192), &tmW, fb, nb * SBN + 64, kb * SBK);
+          if (waited)
+            tma_load_2d(smem_u32(sA + stage * a_stage), &tmA, fb, kb * SBK, 0);
+          else
+            pre_kb[pre++] = kb;  // stage == pre here
+          armed |= 1u << stage;
+          armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == p.stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        const uint32_t fb = smem_u32(&ctl->full[stage]);
-        mbar_arrive_expect_tx(fb, W_STAGE + a_stage);
-        tma_load_2d(smem_u32(sW + stage * W_STAGE), &tmW, fb, nb * SBN, kb * SBK);
-        tma_load_2d(smem_u32(sW + stage * W_STAGE + 8192), &tmW, fb, nb * SBN + 64, kb * SBK);
-        tma_load_2d(smem_u32(sA + stage * a_stage), &tmA, fb, kb * SBK, 0);
-        armed |= 1u << stage;
-        armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
-        if (++stage == p.stages) {
-          stage = 0;
-          phase ^= 1u;
-        }
+      }
+      if (!waited) {
+        grid_dep_wait();
+        for (int i = 0; i < pre; ++i)
+          tma_load_2d(smem_u32(sA + i * a_stage), &tmA, smem_u32(&ctl->full[i]), pre_kb[i] * SBK, 0);
       }
       if (!ok) {
         for (int s = 0; s < p.stages; ++s)
@@ -243,13 +348,12 @@ __global__ void __launch_bounds__(256, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      int seg = 0;
-      int64_t u = u0;
-      while (u < u1 && ok) {
-        const int nb = static_cast<int>(u / p.kblocks);
-        const int64_t seg_end = min(u1, static_cast<int64_t>(nb + 1) * p.kblocks);
-        const int acc = seg & 1;
-        const uint32_t use = static_cast<uint32_t>(seg >> 1);
+      for (int si = 0; si < segs.n && ok; ++si) {
+        int64_t s0, e0;
+        int nb;
+        seg_range(segs, si, &s0, &e0, &nb);
+        const int acc = si & 1;
+        const uint32_t use = static_cast<uint32_t>(si >> 1);
         if (!mbar_wait(smem_u32(&ctl->tempty[acc]), (use & 1u) ^ 1u, &ctl->abort, p.timeout_ns)) {
           raise_abort(ctl, p.status);
           ok = false;
@@ -258,7 +362,7 @@ __global__ void __launch_bounds__(256, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * p.Mpad);
         bool first = true;
-        for (; u < seg_end; ++u) {
+        for (int64_t u = s0; u < e0; ++u) {
           if (!mbar_wait(smem_u32(&ctl->full[stage]), phase, &ctl->abort, p.timeout_ns)) {
             raise_abort(ctl, p.status);
             ok = false;
@@ -281,7 +385,6 @@ __global__ void __launch_bounds__(256, 1)
           }
         }
         if (ok) mma_commit(smem_u32(&ctl->tfull[acc]));
-        ++seg;
       }
       mma_commit(smem_u32(&ctl->drain));
       const uint64_t t0 = global_ns();
@@ -291,15 +394,25 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp >= 4) {
     const int q = warp & 3;
     const int et = threadIdx.x - 128;  // 0..127
-    int seg = 0;
-    int64_t u = u0;
-    while (u < u1) {
-      const int nb = static_cast<int>(u / p.kblocks);
-      const int64_t seg_end = min(u1, static_cast<int64_t>(nb + 1) * p.kblocks);
-      u = seg_end;
-      const int acc = seg & 1;
-      const uint32_t use = static_cast<uint32_t>(seg >> 1);
-      ++seg;
+    grid_dep_wait();  // the accumulators, counters and row scales come from the preceding grids
+    for (int si = 0; si < segs.n; ++si) {
+      int64_t s0, e0;
+      int nb;
+      seg_range(segs, si, &s0, &e0, &nb);
+      const int acc = si & 1;
+      const uint32_t use = static_cast<uint32_t>(si >> 1);
+      // What a finisher of this column block reads besides the accumulator,
+      // loaded while the block's MMAs run.
+      const int nf = nb * SBN + et;
+      uint32_t res[kResRegs];
+      float bias = 0.0f;
+      if ((p.mode == kStreamFinishDown || p.mode == kStreamTpReduce) && nf < p.N) {
+        load_residual(p, nf, res);
+      } else {
+#pragma unroll
+        for (int i = 0; i < kResRegs; ++i) res[i] = 0u;
+        if (p.mode == kStreamFinishUp && p.bias && nf < p.N) bias = __bfloat162float(p.bias[nf]);
+      }
       if (!epi_wait(smem_u32(&ctl->tfull[acc]), use & 1u, ctl, p)) break;
       tc_fence_after();
       const int n = nb * SBN + q * 32 + lane;
@@ -311,7 +424,7 @@ __global__ void __launch_bounds__(256, 1)
         if (n < p.N) {
           // Tensor-parallel reduction: the partial goes straight into the owning
           // rank's accumulator (an NVLink peer address unless this rank owns it).
-          float* dst = p.mode == kStreamTpReduce ? p.tp.acc[nb % p.tp.world] : p.acc;
+          float* dst = p.mode == kStreamTpReduce ? tp_pick(p.tp.acc, nb % p.tp.world) : p.acc;
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int m = c0 + j;
@@ -323,48 +436,49 @@ __global__ void __launch_bounds__(256, 1)
       mbar_arrive(smem_u32(&ctl->tempty[acc]));
       if (p.mode == kStreamPartial) continue;
       if (p.mode == kStreamTpReduce) {
-        tp_arrive_and_finish(p, ctl, nb, et, G);
+        tp_arrive_and_finish(p, ctl, nb, et, G, res);
         continue;
       }
       // Arrive on the column block's counter; the last contributor finishes it.
-      __threadfence();
+      // One thread orders the block's atomics before the arrival (its fence
+      // after the barrier covers the other threads' atomics) and, for the
+      // finisher, the arrivals before the reads.
       epi_bar();
       if (et == 0) {
         const int64_t first_u = static_cast<int64_t>(nb) * p.kblocks;
         const int contributors =
             cta_of(first_u + p.kblocks - 1, p.units, G) - cta_of(first_u, p.units, G) + 1;
+        __threadfence();
         const int prev = atomicAdd(p.counters + nb, 1);
-        ctl->finisher = (prev == contributors - 1);
+        const bool fin = prev == contributors - 1;
+        if (fin) __threadfence();
+        ctl->finisher = fin;
       }
       epi_bar();
       if (ctl->finisher) {
-        __threadfence();
-        const int nf = nb * SBN + et;
         if (nf < p.N) {
-          const float bias = (p.mode == kStreamFinishUp && p.bias) ? __bfloat162float(p.bias[nf]) : 0.0f;
-          // Eight rows per step so their loads are in flight together.
-          for (int m0 = 0; m0 < p.M; m0 += 8) {
-            float val[8], add[8];
+          // Sixteen rows per step so their loads are in flight together.
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+          for (int m0 = 0; m0 < kStreamMaxRows; m0 += 16) {
+            if (m0 >= p.M) break;
+            float val[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
               const int m = m0 + j;
               val[j] = m < p.M ? __ldcg(p.acc + static_cast<int64_t>(m) * p.N + nf) : 0.0f;
-              if (p.mode == kStreamFinishUp)
-                add[j] = m < p.M ? __ldg(p.col_scale + m) : 0.0f;
-              else
-                add[j] = m < p.M ? __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ldr + nf]) : 0.0f;
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < 16; ++j) {
               const int m = m0 + j;
+              if (m >= p.M) break;
               float v = val[j];
               if (p.mode == kStreamFinishUp) {
-                v = v * add[j] + bias;
+                v = v * __ldg(p.col_scale + m) + bias;
                 v = p.gelu == kGeluErf ? gelu_erf(v) : (p.gelu == kGeluTanh ? gelu_tanh(v) : v);
               } else {
-                v += add[j];
+                v += residual_at(res, m);
               }
-              if (m < p.M) p.out[static_cast<int64_t>(m) * p.ldo + nf] = __float2bfloat16_rn(v);
+              p.out[static_cast<int64_t>(m) * p.ldo + nf] = __float2bfloat16_rn(v);
             }
           }
         }
@@ -377,7 +491,7 @@ __global__ void __launch_bounds__(256, 1)
   // (finished on whichever rank) has landed here. One thread waits, bounded.
   if (p.mode == kStreamTpReduce && blockIdx.x == 0 && threadIdx.x == 0) {
     const unsigned target = (p.tp.epoch + 1u) * static_cast<unsigned>(p.nblocks);
-    const volatile unsigned* done = p.tp.done[p.tp.rank];
+    const volatile unsigned* done = tp_pick(p.tp.done, p.tp.rank);
     const uint64_t t0 = global_ns();
     while (static_cast<int>(*done - target) < 0) {
       if (global_ns() - t0 > p.timeout_ns) {
@@ -402,8 +516,8 @@ int stream_mpad(int64_t m) { return static_cast<int>((m + 31) / 32 * 32); }
 size_t stream_counter_bytes(int64_t n) { return static_cast<size_t>((n + SBN - 1) / SBN) * sizeof(int); }
 
 int run_stream(const StreamProblem& sp, cudaStream_t stream, std::string* err) {
-  if (sp.M <= 0 || sp.M > 256 || sp.N <= 0 || sp.K <= 0) {
-    if (err) *err = "weight-streaming GEMM: needs 1 <= M <= 256 and N, K > 0";
+  if (sp.M <= 0 || sp.M > kStreamMaxRows || sp.N <= 0 || sp.K <= 0) {
+    if (err) *err = "weight-streaming GEMM: needs 1 <= M <= 64 and N, K > 0";
     return -2;
   }
   if ((reinterpret_cast<uintptr_t>(sp.A) & 15u) || (reinterpret_cast<uintptr_t>(sp.W) & 15u) || sp.lda % 8 ||
@@ -463,8 +577,24 @@ int run_stream(const StreamProblem& sp, cudaStream_t stream, std::string* err) {
     attr_set[dev] = true;
   }
   const int grid = p.units < sm_count() ? p.units : sm_count();
-  k_stream<<<grid, 256, smem, stream>>>(tw, ta, p);
-  const cudaError_t e = cudaGetLastError();
+  // Programmatic dependent launch: this grid's prologue and first ring of
+  // weight tiles overlap the tail of the preceding grid (TFB200_PDL=0 turns it off).
+  static const bool pdl = [] {
+    const char* v = std::getenv("TFB200_PDL");
+    return !(v && v[0] == '0');
+  }();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_stream, tw, ta, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     if (err) *err = std::string("weight-streaming GEMM launch: ") + cudaGetErrorString(e);
     return -3;
