@@ -128,33 +128,35 @@ int tfb200_fused_mlp_partial(const tfb200_mat* x, const void* gamma, const tfb20
                              size_t workspace_bytes);
 
 /* Tensor-parallel fused MLP with the all-reduce fused into the down-projection
- * kernel (NVLink peer memory instead of a separate collective). Column block nb
- * (128 output columns) is owned by rank nb % world; every rank adds its fp32
- * partial sums straight into the owner's accumulator (peer atomics), the last
- * contributor over all ranks adds the residual, rounds to bf16, writes the
- * block to every rank's output and clears the owner's accumulator; the call
- * returns (stream-ordered) once every block has reached this rank.
- * The caller allocates on every rank, zero-filled before the first call, one
- * buffer of tfb200_tp_buffer_bytes(m, n) and shares it (tfb200_ipc_*), then fills
- * `comm` with each rank's pointers (tfb200_tp_layout). `epoch` counts the calls
- * made with these buffers and must be the same on every rank. All ranks must make
- * the same calls with the same shapes. Waits are bounded (TFB200_ETIMEOUT in the
- * device status word). Same arguments otherwise as tfb200_fused_mlp_partial plus
- * the residual; the result is out[rank] (bf16 [M, N], leading dimension N).
- * No counterpart in the reference, which has no multi-device path. */
+ * kernel (NVLink peer memory instead of a separate collective). W1 is split by
+ * columns (b1 alongside) and W2 by rows; every rank passes the full X, gamma
+ * and residual. Each rank sums its partial products for a 128-column block in
+ * its own buffer; on the other ranks the CTA completing the block pushes it
+ * (fp32, 16-byte stores) into its slot on the block's owner (rank block % world)
+ * and arrives there; the owner waits for them, adds the ranks' sums in rank
+ * order and the residual, rounds to bf16 and writes the block to every rank's
+ * output. The call returns
+ * (stream-ordered) once every block has reached this rank; the result is this
+ * rank's output buffer (tfb200_tp_output), valid until the next call.
+ * Every rank allocates one buffer of tfb200_tp_buffer_bytes(max_rows, n, world)
+ * bytes, 256-byte aligned and zero-filled before the first call, shares it
+ * (tfb200_ipc_*), and fills `peer_buf` with every rank's buffer as mapped in
+ * this process. The kernels return the buffers to zero after each call. All
+ * ranks make the same calls with the same shapes, in the same order. Waits are
+ * bounded: a timeout sets TFB200_ETIMEOUT in the device status word and leaves
+ * the buffers to be zero-filled again. Needs M <= max_rows <= 64, N % 8 == 0,
+ * H % 8 == 0 and 16-byte aligned weights and residual with leading dimensions
+ * % 8 == 0. No counterpart in the reference, which has no multi-device path. */
 #define TFB200_MAX_TP 8
 typedef struct tfb200_tp_comm {
   int32_t rank;
   int32_t world;
-  uint32_t epoch;
-  float* acc[TFB200_MAX_TP];      /* per rank: fp32 [M, N] accumulator */
-  int32_t* counters[TFB200_MAX_TP]; /* per rank: ceil(N/128) arrival counters */
-  void* out[TFB200_MAX_TP];       /* per rank: bf16 [M, N] result */
-  uint32_t* done[TFB200_MAX_TP];  /* per rank: completion counter */
+  int64_t max_rows;                  /* rows the buffers were sized for */
+  void* peer_buf[TFB200_MAX_TP];     /* each rank's buffer, as mapped in this process */
 } tfb200_tp_comm;
-size_t tfb200_tp_buffer_bytes(int64_t m, int64_t n);
-/* Offsets of acc / counters / out / done inside one tfb200_tp_buffer_bytes buffer. */
-int tfb200_tp_layout(int64_t m, int64_t n, size_t* acc_off, size_t* counters_off, size_t* out_off, size_t* done_off);
+size_t tfb200_tp_buffer_bytes(int64_t max_rows, int64_t n, int32_t world);
+/* This rank's bf16 [M, n] result inside its buffer (leading dimension n). */
+int tfb200_tp_output(const tfb200_tp_comm* comm, int64_t n, void** out);
 int tfb200_fused_mlp_tp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w1_shard, const void* b1_shard,
                         const tfb200_mat* w2_shard, const tfb200_mat* residual, float eps, int gelu_mode,
                         const tfb200_tp_comm* comm, void* stream, void* workspace, size_t workspace_bytes);

@@ -68,3 +68,19 @@ def test_host_validation_needs_no_device(L):
     f32 = L.Mat(None, 4, 8, 8, L.TFB200_F32)
     assert lib.tfb200_matmul(ctypes.byref(f32), ctypes.byref(a), ctypes.byref(c), None) == L.TFB200_EINVAL
     assert lib.tfb200_fused_mlp(None, None, None, None, None, None, 1e-5, 0, None, None, None, 0) == L.TFB200_EINVAL
+
+
+def test_tp_buffer_sizes():
+    """One rank's tensor-parallel buffer: local sums, counters, a slot per rank, arrivals, output, done word."""
+    from tfb200 import _lib as L
+
+    lib = L.lib()
+    al = lambda b: (b + 255) // 256 * 256  # noqa: E731
+    for rows, n, world in [(32, 8192, 2), (64, 8192, 8), (1, 8, 1), (7, 1000, 3)]:
+        blocks = (n + 127) // 128
+        want = (al(rows * n * 4) + al(blocks * 4) + world * al(rows * n * 4) + al(blocks * 4) + al(rows * n * 2)
+                + 256)
+        assert lib.tfb200_tp_buffer_bytes(rows, n, world) == want
+    assert lib.tfb200_tp_buffer_bytes(65, 8192, 2) == 0
+    assert lib.tfb200_tp_buffer_bytes(32, 8192, 9) == 0
+    assert lib.tfb200_tp_buffer_bytes(32, 8192, 0) == 0

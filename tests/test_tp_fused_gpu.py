@@ -63,7 +63,7 @@ def test_fused_tp_single_rank_many_calls():
             y = mlp(x, x).float().cpu().numpy()
             res = parity(y, _golden(t, gelu))
             assert res["ok"], (gelu, m, res)
-        assert mlp.comm.epoch == len(ROWS)
+        assert mlp.calls == len(ROWS)
     torch.cuda.synchronize()
     assert lib.tfb200_device_status() == L.TFB200_OK
 
@@ -80,10 +80,14 @@ def test_fused_tp_rejects_bad_communicator():
     comm.rank, comm.world = 2, 2
     with pytest.raises(L.TFB200Error):
         ops.fused_mlp_tp(x, g, w1, b1, w2, x, comm)
-    comm.rank, comm.world = 0, 1  # peer buffers missing
+    comm.rank, comm.world, comm.max_rows = 0, 1, 64  # peer buffers missing
     with pytest.raises(L.TFB200Error):
         ops.fused_mlp_tp(x, g, w1, b1, w2, x, comm)
-    assert ctypes.c_size_t(L.lib().tfb200_tp_buffer_bytes(0, 8)).value == 0
+    comm.max_rows = 2  # fewer rows than the call has
+    with pytest.raises(L.TFB200Error):
+        ops.fused_mlp_tp(x, g, w1, b1, w2, x, comm)
+    assert ctypes.c_size_t(L.lib().tfb200_tp_buffer_bytes(0, 8, 1)).value == 0
+    assert ctypes.c_size_t(L.lib().tfb200_tp_buffer_bytes(65, 8, 1)).value == 0
 
 
 def _rank_main(rank, world, port, out_dir):
@@ -119,7 +123,7 @@ def _rank_main(rank, world, port, out_dir):
 
 
 @pytest.mark.timeout(600)
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_fused_tp_across_gpus(tmp_path, world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs (ranks on one GPU would wait on one another)")

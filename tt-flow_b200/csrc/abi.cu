@@ -376,23 +376,29 @@ int tfb200_selftest_bounded_wait(uint64_t limit_ns, void* stream) {
 
 static size_t al256b(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
 
-int tfb200_tp_layout(int64_t m, int64_t n, size_t* acc_off, size_t* counters_off, size_t* out_off, size_t* done_off) {
-  if (m <= 0 || n <= 0) return fail(TFB200_EINVAL, "tfb200_tp_layout: empty shape");
-  const size_t acc = 0;
-  const size_t cnt = acc + al256b(static_cast<size_t>(m) * n * 4);
-  const size_t out = cnt + al256b(static_cast<size_t>((n + 127) / 128) * 4);
-  const size_t done = out + al256b(static_cast<size_t>(m) * n * 2);
-  if (acc_off) *acc_off = acc;
-  if (counters_off) *counters_off = cnt;
-  if (out_off) *out_off = out;
-  if (done_off) *done_off = done;
-  return TFB200_OK;
-}
+}  // extern "C"
 
-size_t tfb200_tp_buffer_bytes(int64_t m, int64_t n) {
-  size_t done = 0;
-  if (tfb200_tp_layout(m, n, nullptr, nullptr, nullptr, &done) != TFB200_OK) return 0;
-  return done + 256;
+namespace tfb200 {
+TpLayout tp_layout(int64_t max_rows, int64_t n, int world) {
+  TpLayout l{};
+  const size_t rows_n = static_cast<size_t>(max_rows) * static_cast<size_t>(n);
+  const size_t blocks = static_cast<size_t>((n + 127) / 128);
+  l.acc = 0;
+  l.local_cnt = l.acc + al256b(rows_n * 4);
+  l.slots = l.local_cnt + al256b(blocks * 4);
+  l.arrive = l.slots + static_cast<size_t>(world) * al256b(rows_n * 4);
+  l.out = l.arrive + al256b(blocks * 4);
+  l.done = l.out + al256b(rows_n * 2);
+  l.total = l.done + 256;
+  return l;
+}
+}  // namespace tfb200
+
+extern "C" {
+
+size_t tfb200_tp_buffer_bytes(int64_t max_rows, int64_t n, int32_t world) {
+  if (max_rows <= 0 || max_rows > kStreamMaxRows || n <= 0 || world < 1 || world > TFB200_MAX_TP) return 0;
+  return tp_layout(max_rows, n, world).total;
 }
 
 int tfb200_fused_mlp_tp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w1, const void* b1,
@@ -411,30 +417,47 @@ int tfb200_fused_mlp_tp(const tfb200_mat* x, const void* gamma, const tfb200_mat
     return fail(TFB200_EINVAL, "tfb200_fused_mlp_tp: bad gelu_mode");
   if (!(eps >= 0.0f) || !gamma || K == 0) return fail(TFB200_EINVAL, "tfb200_fused_mlp_tp: bad eps / gamma / K");
   if (M == 0 || N == 0) return TFB200_OK;
+  if (M > comm->max_rows || comm->max_rows > kStreamMaxRows)
+    return fail(TFB200_EINVAL, "tfb200_fused_mlp_tp: more rows than the buffers were sized for (max_rows <= 64)");
   for (int r = 0; r < comm->world; ++r)
-    if (!comm->acc[r] || !comm->counters[r] || !comm->out[r] || !comm->done[r])
-      return fail(TFB200_EINVAL, "tfb200_fused_mlp_tp: missing peer buffer");
-  if (!decode_eligible(M, w1->data, w1->ld, w2->data, w2->ld) || H % 8 != 0)
+    if (!comm->peer_buf[r] || (reinterpret_cast<uintptr_t>(comm->peer_buf[r]) & 255u))
+      return fail(TFB200_EINVAL, "tfb200_fused_mlp_tp: missing or unaligned peer buffer");
+  if (!decode_eligible(M, w1->data, w1->ld, w2->data, w2->ld) || H % 8 != 0 || N % 8 != 0 ||
+      (reinterpret_cast<uintptr_t>(residual->data) & 15u) || residual->ld % 8 != 0)
     return fail(TFB200_EUNSUPPORTED,
-                "tfb200_fused_mlp_tp: needs M <= 64, 16-byte aligned weights with ld % 8 == 0, H % 8 == 0");
+                "tfb200_fused_mlp_tp: needs 16-byte aligned weights and residual with leading dimensions % 8 == 0, "
+                "H % 8 == 0 and N % 8 == 0");
   const size_t need = tfb200_fused_mlp_partial_workspace_size(M, K, H, N);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return fail(TFB200_EWORKSPACE, "tfb200_fused_mlp_tp: workspace missing, small or not 256-byte aligned");
+  const TpLayout l = tp_layout(comm->max_rows, N, comm->world);
   TpPeers tp;
   tp.rank = comm->rank;
   tp.world = comm->world;
-  tp.epoch = comm->epoch;
+  tp.slot_stride = comm->max_rows * N;
+  char* own = static_cast<char*>(comm->peer_buf[comm->rank]);
+  tp.acc = reinterpret_cast<float*>(own + l.acc);
+  tp.local_cnt = reinterpret_cast<int*>(own + l.local_cnt);
   for (int r = 0; r < comm->world; ++r) {
-    tp.acc[r] = comm->acc[r];
-    tp.cnt[r] = comm->counters[r];
-    tp.out[r] = static_cast<bf16*>(comm->out[r]);
-    tp.done[r] = comm->done[r];
+    char* b = static_cast<char*>(comm->peer_buf[r]);
+    tp.slots[r] = reinterpret_cast<float*>(b + l.slots);
+    tp.arrive[r] = reinterpret_cast<unsigned*>(b + l.arrive);
+    tp.out[r] = reinterpret_cast<bf16*>(b + l.out);
+    tp.done[r] = reinterpret_cast<unsigned*>(b + l.done);
   }
   const int rc = run_decode_mlp(as_bf16(x->data), x->ld, as_bf16(gamma), as_bf16(w1->data), w1->ld, as_bf16(b1),
                                 as_bf16(w2->data), w2->ld, as_bf16(residual->data), residual->ld, eps,
                                 gelu_mode == TFB200_GELU_ERF ? kGeluErf : kGeluTanh, nullptr, 0, nullptr, 0, M, K, H,
                                 N, workspace, static_cast<cudaStream_t>(stream), &err, &tp);
   return rc ? fail(rc, "tfb200_fused_mlp_tp: " + err) : TFB200_OK;
+}
+
+int tfb200_tp_output(const tfb200_tp_comm* comm, int64_t n, void** out) {
+  if (!comm || !out || comm->world < 1 || comm->world > TFB200_MAX_TP || comm->rank < 0 ||
+      comm->rank >= comm->world || !comm->peer_buf[comm->rank] || n <= 0)
+    return fail(TFB200_EINVAL, "tfb200_tp_output: bad communicator");
+  *out = static_cast<char*>(comm->peer_buf[comm->rank]) + tp_layout(comm->max_rows, n, comm->world).out;
+  return TFB200_OK;
 }
 
 int tfb200_ipc_get(const void* ptr, void* handle64, size_t* offset) {

@@ -121,10 +121,13 @@ int run_decode_mlp(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* w1
   dn.acc = acc2;
   dn.counters = cnt2;
   if (tp) {
-    // Down-projection and the cross-GPU reduction in one kernel; the peers'
-    // accumulators clean themselves, so nothing to clear here.
+    // Down-projection and the cross-GPU reduction in one kernel. Its local
+    // sums and counters live in the tensor-parallel buffer and are returned to
+    // zero by the kernel, so nothing to clear here.
     dn.mode = kStreamTpReduce;
     dn.tp = *tp;
+    dn.acc = tp->acc;
+    dn.counters = tp->local_cnt;
     dn.residual = residual;
     dn.ldr = ldr;
     dn.ldo = N;

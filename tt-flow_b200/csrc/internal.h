@@ -43,20 +43,30 @@ int run_gemm(const GemmProblem& p, cudaStream_t stream, std::string* err);
 // split over all SMs, then a per-column-block finishing epilogue.
 enum StreamMode : int { kStreamPartial = 0, kStreamFinishUp = 1, kStreamFinishDown = 2, kStreamTpReduce = 3 };
 constexpr int kMaxTp = 8;
-// Peer buffers of the tensor-parallel reduction fused into the down-projection
-// (kStreamTpReduce). Column block nb of the output is owned by rank nb % world:
-// every rank adds its fp32 partial into the owner's accumulator over NVLink, the
-// last contributor (across all ranks) adds the residual, rounds, writes the block
-// to every rank's output, clears the owner's accumulator and bumps every rank's
-// done counter. Counters are monotonic: `epoch` numbers the calls.
+// Tensor-parallel reduction fused into the down-projection (kStreamTpReduce).
+// Each rank first sums its CTAs' partials for a 128-column block in its own
+// accumulator (L2 atomics). On a rank that does not own the block (owner =
+// nb % world), the CTA that completes it locally pushes it, M x 128 fp32 in
+// 16-byte stores, into its slot on the owner and arrives on the owner's
+// counter. On the owner, that CTA waits for the other ranks' arrivals, adds
+// the slots and its own sums in rank order plus the residual, rounds, writes
+// the block to every rank's output and bumps every rank's done counter.
+// Counters and accumulators are returned to zero by the CTAs done with them.
 struct TpPeers {
   int rank = 0, world = 1;
-  uint32_t epoch = 0;
-  float* acc[kMaxTp] = {};
-  int* cnt[kMaxTp] = {};
-  bf16* out[kMaxTp] = {};
-  unsigned int* done[kMaxTp] = {};
+  int64_t slot_stride = 0;          // elements between two source slots (rows capacity x N)
+  float* acc = nullptr;             // this rank: fp32 [M, N] local sums
+  int* local_cnt = nullptr;         // this rank: per-block local arrivals
+  float* slots[kMaxTp] = {};        // per rank: `world` fp32 [M, N] slots, one per source rank
+  unsigned int* arrive[kMaxTp] = {};  // per rank: per-block arrivals of the ranks
+  bf16* out[kMaxTp] = {};           // per rank: bf16 [M, N] result
+  unsigned int* done[kMaxTp] = {};  // per rank: blocks finished for it in this call
 };
+// Byte offsets of one rank's tensor-parallel buffer (all 256-byte aligned).
+struct TpLayout {
+  size_t acc, local_cnt, slots, arrive, out, done, total;
+};
+TpLayout tp_layout(int64_t max_rows, int64_t n, int world);
 struct StreamProblem {
   int64_t M = 0, N = 0, K = 0;
   const bf16* A = nullptr;  // [M, K] tokens

@@ -81,6 +81,32 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const v
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Counter updates with release / acquire semantics. Called by one thread after
+// a CTA barrier: the release covers the memory operations the other threads
+// made before the barrier, the acquire orders the reads they make after the
+// next barrier.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* ptr, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(ptr), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ unsigned atom_add_acq_rel_sys(unsigned* ptr, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(ptr), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void red_add_release_sys(unsigned* ptr, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* ptr) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys(unsigned* ptr, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
 // fp32 load with system-scope relaxed semantics (another GPU may have written it).
 __device__ __forceinline__ float ld_relaxed_sys(const float* ptr) {
   float v;

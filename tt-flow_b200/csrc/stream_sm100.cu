@@ -175,64 +175,156 @@ __device__ __forceinline__ T* tp_pick(T* const (&arr)[kMaxTp], int i) {
   return r;
 }
 
-// Cross-GPU arrival on column block nb and, for the last contributor over all
-// ranks, the finish: residual, bf16, store to every rank, clear the owner's
-// accumulator, bump every rank's done counter. Called by the 128 epilogue
-// threads after their atomics on the owner's accumulator. One thread orders
-// the block's memory operations at system scope (a fence after the barrier
-// covers what the other threads did before it).
-__device__ __forceinline__ void tp_arrive_and_finish(const SParams& p, SCtl* ctl, int nb, int et, int G,
-                                                     const uint32_t (&res)[kResRegs]) {
+// Tensor-parallel finish mapping: epilogue thread et covers the 8 columns
+// nb*128 + (et % 16)*8 .. +8 of rows et/16 + 8k, so every access is a 16-byte
+// vector. Its residual values, bf16 pairs: res[4k + i] = columns 2i, 2i+1 of
+// row et/16 + 8k.
+__device__ __forceinline__ void load_residual_tp(const SParams& p, int nb, int et, uint32_t (&res)[kResRegs]) {
+  const int r0 = et >> 4;
+  const int c = nb * SBN + (et & 15) * 8;
+#pragma unroll
+  for (int k = 0; k < kStreamMaxRows / 8; ++k) {
+    const int m = r0 + 8 * k;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (m < p.M && c < p.N) v = __ldg(reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(m) * p.ldr + c));
+    res[4 * k + 0] = v.x;
+    res[4 * k + 1] = v.y;
+    res[4 * k + 2] = v.z;
+    res[4 * k + 3] = v.w;
+  }
+}
+
+__device__ __forceinline__ float4 ld_relaxed_sys_v4(const float* ptr) {
+  float4 v;
+  asm volatile("ld.relaxed.sys.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(ptr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
+  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+  return a | (b << 16);
+}
+__device__ __forceinline__ float bf16_lo_f(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16_hi_f(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+
+// Called by the 128 epilogue threads of the CTA that completed column block nb
+// on this rank. Another rank pushes its sums into its slot on the block's
+// owner and arrives there (release); the owner waits until the other ranks
+// have arrived (acquire, bounded), adds their slots and its own sums in rank
+// order plus the residual, writes the block to every rank and counts it done
+// there (release). One thread arrives or waits for the CTA, after a barrier.
+__device__ __forceinline__ void tp_push_and_finish(const SParams& p, SCtl* ctl, int nb, int et,
+                                                   const uint32_t (&res)[kResRegs]) {
   const int owner = nb % p.tp.world;
-  epi_bar();
+  const int r0 = et >> 4;
+  const int c = nb * SBN + (et & 15) * 8;
+  const bool col_ok = c < p.N;
+  constexpr int kRows = kStreamMaxRows / 8;
+  if (owner != p.tp.rank) {
+    float* slot = tp_pick(p.tp.slots, owner) + static_cast<int64_t>(p.tp.rank) * p.tp.slot_stride;
+#pragma unroll
+    for (int k = 0; k < kRows; ++k) {
+      const int m = r0 + 8 * k;
+      if (m < p.M && col_ok) {
+        float* src = p.acc + static_cast<int64_t>(m) * p.N + c;
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(src));
+        const float4 b = __ldcg(reinterpret_cast<const float4*>(src + 4));
+        float* dst = slot + static_cast<int64_t>(m) * p.N + c;
+        *reinterpret_cast<float4*>(dst) = a;
+        *reinterpret_cast<float4*>(dst + 4) = b;
+        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(src) = z;  // ready for the next call
+        *reinterpret_cast<float4*>(src + 4) = z;
+      }
+    }
+    epi_bar();
+    if (et == 0) {
+      p.counters[nb] = 0;  // every local contribution is in: ready for the next call
+      red_add_release_sys(tp_pick(p.tp.arrive, owner) + nb, 1u);  // the slot before the arrival
+    }
+    return;
+  }
+  // Owner: its own sums, read before the wait.
+  float own[kRows][8];
+#pragma unroll
+  for (int k = 0; k < kRows; ++k) {
+    const int m = r0 + 8 * k;
+    if (m < p.M && col_ok) {
+      float* src = p.acc + static_cast<int64_t>(m) * p.N + c;
+      const float4 a = __ldcg(reinterpret_cast<const float4*>(src));
+      const float4 b = __ldcg(reinterpret_cast<const float4*>(src + 4));
+      own[k][0] = a.x; own[k][1] = a.y; own[k][2] = a.z; own[k][3] = a.w;
+      own[k][4] = b.x; own[k][5] = b.y; own[k][6] = b.z; own[k][7] = b.w;
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(src) = z;  // ready for the next call
+      *reinterpret_cast<float4*>(src + 4) = z;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) own[k][i] = 0.f;
+    }
+  }
   if (et == 0) {
-    const int64_t first_u = static_cast<int64_t>(nb) * p.kblocks;
-    const unsigned per_rank =
-        static_cast<unsigned>(cta_of(first_u + p.kblocks - 1, p.units, G) - cta_of(first_u, p.units, G) + 1);
-    const unsigned total = per_rank * static_cast<unsigned>(p.tp.world);
-    __threadfence_system();  // the block's partial sums before its arrival
-    const unsigned prev = atomicAdd_system(reinterpret_cast<unsigned*>(tp_pick(p.tp.cnt, owner)) + nb, 1u);
-    const bool fin = prev + 1u == (p.tp.epoch + 1u) * total;
-    if (fin) __threadfence_system();  // every rank's partial sums before the reads
-    ctl->finisher = fin;
+    p.counters[nb] = 0;
+    unsigned* arr = tp_pick(p.tp.arrive, owner) + nb;
+    const unsigned want = static_cast<unsigned>(p.tp.world - 1);
+    const uint64_t t0 = global_ns();
+    bool ok = true;
+    while (ld_acquire_sys(arr) < want) {
+      if (global_ns() - t0 > p.timeout_ns) {
+        atomicExch(p.status, kDevTimeout);
+        ok = false;
+        break;
+      }
+    }
+    if (ok) st_relaxed_sys(arr, 0u);  // every rank is in: ready for the next call
+    ctl->finisher = ok;
   }
   epi_bar();
   if (!ctl->finisher) return;
-  float* accp = tp_pick(p.tp.acc, owner);
+  const float* slots = tp_pick(p.tp.slots, owner);
   bf16* outs[kMaxTp];
 #pragma unroll
   for (int r = 0; r < kMaxTp; ++r) outs[r] = r < p.tp.world ? p.tp.out[r] : nullptr;
-  const int nf = nb * SBN + et;
-  if (nf < p.N) {
-    // Sixteen rows per step: the accumulator may be a peer's, one NVLink round
-    // trip per step.
 #pragma unroll
-    for (int m0 = 0; m0 < kStreamMaxRows; m0 += 16) {
-      if (m0 >= p.M) break;
-      float val[16];
+  for (int k = 0; k < kRows; ++k) {
+    const int m = r0 + 8 * k;
+    if (m < p.M && col_ok) {
+      // The ranks' sums in rank order (the same on every run), then the residual.
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int m = m0 + j;
-        val[j] = m < p.M ? ld_relaxed_sys(accp + static_cast<int64_t>(m) * p.N + nf) : 0.0f;
+      for (int r = 0; r < kMaxTp; ++r) {
+        if (r >= p.tp.world) break;
+        if (r == owner) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] += own[k][i];
+        } else {
+          const float* src = slots + static_cast<int64_t>(r) * p.tp.slot_stride + static_cast<int64_t>(m) * p.N + c;
+          const float4 a = ld_relaxed_sys_v4(src);
+          const float4 b = ld_relaxed_sys_v4(src + 4);
+          acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+          acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+        }
       }
+      uint4 o;
+      o.x = pack2_bf16(acc[0] + bf16_lo_f(res[4 * k + 0]), acc[1] + bf16_hi_f(res[4 * k + 0]));
+      o.y = pack2_bf16(acc[2] + bf16_lo_f(res[4 * k + 1]), acc[3] + bf16_hi_f(res[4 * k + 1]));
+      o.z = pack2_bf16(acc[4] + bf16_lo_f(res[4 * k + 2]), acc[5] + bf16_hi_f(res[4 * k + 2]));
+      o.w = pack2_bf16(acc[6] + bf16_lo_f(res[4 * k + 3]), acc[7] + bf16_hi_f(res[4 * k + 3]));
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int m = m0 + j;
-        if (m >= p.M) break;
-        const bf16 o = __float2bfloat16_rn(val[j] + residual_at(res, m));
-#pragma unroll
-        for (int r = 0; r < kMaxTp; ++r)
-          if (r < p.tp.world) outs[r][static_cast<int64_t>(m) * p.ldo + nf] = o;
-        accp[static_cast<int64_t>(m) * p.N + nf] = 0.0f;  // ready for the next call
-      }
+      for (int r = 0; r < kMaxTp; ++r)
+        if (r < p.tp.world) *reinterpret_cast<uint4*>(outs[r] + static_cast<int64_t>(m) * p.ldo + c) = o;
     }
   }
   epi_bar();
   if (et == 0) {
-    __threadfence_system();  // the block's rows on every rank before the done counts
+    // Release: the block's rows on every rank before its done counts.
 #pragma unroll
     for (int r = 0; r < kMaxTp; ++r)
-      if (r < p.tp.world) atomicAdd_system(p.tp.done[r], 1u);
+      if (r < p.tp.world) red_add_release_sys(p.tp.done[r], 1u);
   }
 }
 
@@ -406,8 +498,10 @@ __global__ void __launch_bounds__(256, 1)
       const int nf = nb * SBN + et;
       uint32_t res[kResRegs];
       float bias = 0.0f;
-      if ((p.mode == kStreamFinishDown || p.mode == kStreamTpReduce) && nf < p.N) {
+      if (p.mode == kStreamFinishDown && nf < p.N) {
         load_residual(p, nf, res);
+      } else if (p.mode == kStreamTpReduce) {
+        load_residual_tp(p, nb, et, res);
       } else {
 #pragma unroll
         for (int i = 0; i < kResRegs; ++i) res[i] = 0u;
@@ -422,39 +516,33 @@ __global__ void __launch_bounds__(256, 1)
                        v);
         tmem_wait_ld();
         if (n < p.N) {
-          // Tensor-parallel reduction: the partial goes straight into the owning
-          // rank's accumulator (an NVLink peer address unless this rank owns it).
-          float* dst = p.mode == kStreamTpReduce ? tp_pick(p.tp.acc, nb % p.tp.world) : p.acc;
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int m = c0 + j;
-            if (m < p.M) atomicAdd(dst + static_cast<int64_t>(m) * p.N + n, __uint_as_float(v[j]));
+            if (m < p.M) atomicAdd(p.acc + static_cast<int64_t>(m) * p.N + n, __uint_as_float(v[j]));
           }
         }
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl->tempty[acc]));
       if (p.mode == kStreamPartial) continue;
-      if (p.mode == kStreamTpReduce) {
-        tp_arrive_and_finish(p, ctl, nb, et, G, res);
-        continue;
-      }
       // Arrive on the column block's counter; the last contributor finishes it.
-      // One thread orders the block's atomics before the arrival (its fence
-      // after the barrier covers the other threads' atomics) and, for the
-      // finisher, the arrivals before the reads.
+      // One thread arrives for the CTA after a barrier.
       epi_bar();
       if (et == 0) {
         const int64_t first_u = static_cast<int64_t>(nb) * p.kblocks;
         const int contributors =
             cta_of(first_u + p.kblocks - 1, p.units, G) - cta_of(first_u, p.units, G) + 1;
-        __threadfence();
-        const int prev = atomicAdd(p.counters + nb, 1);
-        const bool fin = prev == contributors - 1;
-        if (fin) __threadfence();
-        ctl->finisher = fin;
+        // Release: the block's atomics before the arrival; acquire: every
+        // contributor's atomics before the finisher's reads.
+        const int prev = atom_add_acq_rel_gpu(p.counters + nb, 1);
+        ctl->finisher = prev == contributors - 1;
       }
       epi_bar();
+      if (p.mode == kStreamTpReduce) {
+        if (ctl->finisher) tp_push_and_finish(p, ctl, nb, et, res);
+        continue;
+      }
       if (ctl->finisher) {
         if (nf < p.N) {
           // Sixteen rows per step so their loads are in flight together.
@@ -488,18 +576,21 @@ __global__ void __launch_bounds__(256, 1)
   }
 
   // Tensor-parallel: the call is complete on this rank once every column block
-  // (finished on whichever rank) has landed here. One thread waits, bounded.
+  // (finished on whichever rank) has landed here. One thread waits, bounded,
+  // then returns the counter to zero for the next call.
   if (p.mode == kStreamTpReduce && blockIdx.x == 0 && threadIdx.x == 0) {
-    const unsigned target = (p.tp.epoch + 1u) * static_cast<unsigned>(p.nblocks);
-    const volatile unsigned* done = tp_pick(p.tp.done, p.tp.rank);
+    unsigned* done = tp_pick(p.tp.done, p.tp.rank);
+    const unsigned target = static_cast<unsigned>(p.nblocks);
     const uint64_t t0 = global_ns();
-    while (static_cast<int>(*done - target) < 0) {
+    bool ok = true;
+    while (ld_acquire_sys(done) < target) {
       if (global_ns() - t0 > p.timeout_ns) {
         atomicExch(p.status, kDevTimeout);
+        ok = false;
         break;
       }
     }
-    __threadfence_system();
+    if (ok) st_relaxed_sys(done, 0u);
   }
   tc_fence_before();
   __syncthreads();

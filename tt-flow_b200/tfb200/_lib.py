@@ -40,7 +40,7 @@ EXPORTS = (
     "tfb200_fused_mlp_partial_workspace_size",
     "tfb200_fused_mlp_partial",
     "tfb200_tp_buffer_bytes",
-    "tfb200_tp_layout",
+    "tfb200_tp_output",
     "tfb200_fused_mlp_tp",
     "tfb200_ipc_get",
     "tfb200_ipc_open",
@@ -72,11 +72,8 @@ class TpComm(ctypes.Structure):
     _fields_ = [
         ("rank", ctypes.c_int32),
         ("world", ctypes.c_int32),
-        ("epoch", ctypes.c_uint32),
-        ("acc", ctypes.c_void_p * MAX_TP),
-        ("counters", ctypes.c_void_p * MAX_TP),
-        ("out", ctypes.c_void_p * MAX_TP),
-        ("done", ctypes.c_void_p * MAX_TP),
+        ("max_rows", ctypes.c_int64),
+        ("peer_buf", ctypes.c_void_p * MAX_TP),
     ]
 
 
@@ -110,8 +107,8 @@ def lib() -> ctypes.CDLL:
         "tfb200_fused_mlp_partial_workspace_size": ([ctypes.c_int64] * 4, sz),
         "tfb200_fused_mlp_partial": ([P, vp, P, vp, P, f32, i32, vp, ctypes.c_int64, vp, vp, sz], i32),
         "tfb200_residual_add": ([vp, ctypes.c_int64, P, P, vp], i32),
-        "tfb200_tp_buffer_bytes": ([ctypes.c_int64, ctypes.c_int64], sz),
-        "tfb200_tp_layout": ([ctypes.c_int64, ctypes.c_int64] + [ctypes.POINTER(ctypes.c_size_t)] * 4, i32),
+        "tfb200_tp_buffer_bytes": ([ctypes.c_int64, ctypes.c_int64, ctypes.c_int32], sz),
+        "tfb200_tp_output": ([ctypes.POINTER(TpComm), ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p)], i32),
         "tfb200_fused_mlp_tp": ([P, vp, P, vp, P, P, f32, i32, ctypes.POINTER(TpComm), vp, vp, sz], i32),
         "tfb200_ipc_get": ([vp, vp, ctypes.POINTER(ctypes.c_size_t)], i32),
         "tfb200_ipc_open": ([vp, ctypes.POINTER(ctypes.c_void_p)], i32),

@@ -112,9 +112,9 @@ def exchange_handles(local: tuple, rank: int, world: int, gather_fn: Callable) -
 class TPDecodeMLPFused:
     """The decode MLP on `world` GPUs with the all-reduce inside the down-projection kernel.
 
-    Every rank allocates one zero-filled buffer (fp32 accumulator, column-block counters, bf16 output, done
-    counter) for up to ``max_rows`` token rows, shares it with CUDA IPC and keeps a call counter (the epoch)
-    that must advance in step on every rank. ``__call__`` returns a view of this rank's output buffer, valid
+    Every rank allocates one zero-filled buffer (local sums and counters, one receive slot per rank, arrival
+    counters, bf16 output, done counter) for up to ``max_rows`` token rows and shares it with CUDA IPC. All ranks
+    must make the same calls in the same order. ``__call__`` returns a view of this rank's output buffer, valid
     until the next call. After a device timeout the buffers are in an unknown state: build a new instance.
     """
 
@@ -134,17 +134,17 @@ class TPDecodeMLPFused:
         self.gamma, self.eps, self.gelu = gamma, eps, gelu
         self.rank, self.world, self.max_rows = rank, world, max_rows
         self.N = w2.shape[1]
+        self.calls = 0
         lib = L.lib()
-        nbytes = int(lib.tfb200_tp_buffer_bytes(max_rows, self.N))
+        nbytes = int(lib.tfb200_tp_buffer_bytes(max_rows, self.N, world))
         if nbytes == 0:
-            raise ValueError("tfb200_tp_buffer_bytes: bad shape")
-        offs = [ctypes.c_size_t() for _ in range(4)]
-        L.check(lib.tfb200_tp_layout(max_rows, self.N, *[ctypes.byref(o) for o in offs]))
-        self.offsets = [o.value for o in offs]
+            raise ValueError("tfb200_tp_buffer_bytes: bad shape (max_rows must be 1..64)")
+        # 256-byte aligned, zero-filled (the caching allocator returns 512-byte aligned blocks)
         self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=w1.device)
         torch.cuda.synchronize(w1.device)
         self._opened = []
         bases = [0] * world
+        bases[rank] = self.buf.data_ptr()
         if world > 1:
             import torch.distributed as dist
 
@@ -160,22 +160,18 @@ class TPDecodeMLPFused:
             peers = exchange_handles((bytes(handle), off.value), rank, world, gather)
             for r, (h, o) in enumerate(peers):
                 if r == rank:
-                    bases[r] = self.buf.data_ptr()
                     continue
                 base = ctypes.c_void_p()
                 L.check(lib.tfb200_ipc_open(ctypes.create_string_buffer(h, 64), ctypes.byref(base)))
                 self._opened.append(base.value)
                 bases[r] = base.value + o
-        else:
-            bases[0] = self.buf.data_ptr()
         self.comm = L.TpComm()
-        self.comm.rank, self.comm.world, self.comm.epoch = rank, world, 0
-        a, c, o, d = self.offsets
+        self.comm.rank, self.comm.world, self.comm.max_rows = rank, world, max_rows
         for r in range(world):
-            self.comm.acc[r] = bases[r] + a
-            self.comm.counters[r] = bases[r] + c
-            self.comm.out[r] = bases[r] + o
-            self.comm.done[r] = bases[r] + d
+            self.comm.peer_buf[r] = bases[r]
+        out = ctypes.c_void_p()
+        L.check(lib.tfb200_tp_output(ctypes.byref(self.comm), self.N, ctypes.byref(out)))
+        o = out.value - self.buf.data_ptr()
         self._out_flat = self.buf[o:o + max_rows * self.N * 2].view(torch.bfloat16)
         self._ws = None
         # Every rank's buffer is zero before any rank's first call.
@@ -192,7 +188,7 @@ class TPDecodeMLPFused:
             self._ws = self.torch.empty(max(need, 256), dtype=self.torch.uint8, device=x.device)
         self.ops.fused_mlp_tp(x, self.gamma, self.shard.w1, self.shard.b1, self.shard.w2, residual, self.comm,
                               self.eps, self.gelu, workspace=self._ws)
-        self.comm.epoch = (self.comm.epoch + 1) & 0xFFFFFFFF
+        self.calls += 1
         return self._out_flat[:M * self.N].view(M, self.N)
 
     def close(self):
