@@ -210,6 +210,16 @@ int tfb200_fused_mlp_noalloc(const tfb200_mat* x, const void* gamma, const tfb20
  * planner in place of the Tensix planner. */
 int tfb200_opt(const char* text, const char* args, char* out, size_t cap, size_t* needed);
 
+/* Re-plan a plan document for the B200: `plan_json_in` is a plan JSON of
+ * schema/plan.schema.json written for any device (tensixflow-translate
+ * --tensixflow-to-json, tools/tensixflow-translate/tensixflow-translate.cpp:75-222,
+ * or tfb200_opt); its `tensors` and `fusion` give the problem. Writes the B200
+ * plan JSON (device b200, mapping, CTAs, shared-memory stages, fused_feasible,
+ * HBM bytes, time estimate) to `out`; `needed` as for tfb200_opt. Malformed
+ * documents give TFB200_EINVAL with the line and column in tfb200_last_error().
+ * No counterpart in the reference, which re-plans only from IR. */
+int tfb200_plan(const char* plan_json_in, char* out, size_t cap, size_t* needed);
+
 /* Device status word of the current device: TFB200_OK, or TFB200_ETIMEOUT if a
  * kernel's bounded wait ran out since the last clear. Synchronises the device. */
 int tfb200_device_status(void);

@@ -129,6 +129,81 @@ def test_c_abi_matches_tool():
     assert b"error" in lib.tfb200_last_error()
 
 
+def _plan(doc: str):
+    from tfb200 import _lib as L
+
+    lib = L.lib()
+    need = ctypes.c_size_t(0)
+    rc = lib.tfb200_plan(doc.encode(), None, 0, ctypes.byref(need))
+    if rc != L.TFB200_ENOSPC:
+        return rc, None, lib.tfb200_last_error().decode()
+    buf = ctypes.create_string_buffer(need.value)
+    rc = lib.tfb200_plan(doc.encode(), buf, need.value, None)
+    return rc, buf.value.decode(), lib.tfb200_last_error().decode()
+
+
+@pytest.mark.parametrize("lit", ["b200_plan_rmsnorm_matmul.mlir", "b200_plan_mlp.mlir", "b200_plan_decode.mlir"])
+def test_plan_json_round_trips_through_tfb200_plan(lit):
+    """A plan written by this front end, re-planned from its JSON, comes back unchanged."""
+    text = (ROOT / "tests" / "lit" / lit).read_text()
+    rc, out, err = _opt(text, "--tensixflow-fuse-rmsnorm-matmul", "--tensixflow-to-json")
+    assert rc == 0, err
+    rc2, again, err2 = _plan(out)
+    assert rc2 == 0, err2
+    assert again == out
+
+
+def _reference_style_doc(fusion, shapes):
+    """A plan document as the reference's translate tool writes it for an n150: function arguments arg0..argN."""
+    tensors = [{"name": f"arg{i}", "shape": s, "dtype": "bf16", "placement": "DRAM"} for i, s in enumerate(shapes)]
+    doc = {"graph_id": "g", "device": {"name": "n150", "arch": "wormhole_b0", "grid_x": 8, "grid_y": 8,
+                                        "l1_usable_bytes": 1499136, "flops_per_cycle_per_core": 2048,
+                                        "dram_bandwidth_bytes_per_second": 288000000000},
+           "tensors": tensors, "layout": {"activation_sharding": "row-major", "weight_strategy": "replicate"},
+           "shard_grid": {"grid_y": 8, "grid_x": 8}, "cb_specs": [], "noc": {}, "emission": {}, "perf": {}, "viz": {}}
+    if fusion:
+        doc["fusion"] = fusion
+    return json.dumps(doc)
+
+
+@pytest.mark.parametrize("fusion,shapes,want", [
+    ("fused_mlp", [[8192, 4096], [4096], [4096, 16384], [16384], [16384, 4096], [8192, 4096]], "fused_mlp"),
+    (None, [[8192, 4096], [4096], [4096, 16384], [16384], [16384, 4096], [8192, 4096]], "fused_mlp"),
+    ("fused_rmsnorm_matmul", [[2, 4096, 4096], [4096], [4096, 6144]], "fused_rmsnorm_matmul"),
+    (None, [[8192, 4096], [4096], [4096, 6144]], "fused_rmsnorm_matmul"),
+    (None, [[256, 512], [512, 1024]], "none"),
+    ("fused_mlp", [[32, 8192], [8192], [8192, 28672], [28672], [28672, 8192], [32, 8192]], "fused_mlp"),
+])
+def test_tfb200_plan_replans_reference_documents(fusion, shapes, want):
+    rc, out, err = _plan(_reference_style_doc(fusion, shapes))
+    assert rc == 0, err
+    plan = json.loads(out)
+    schema = json.loads((ROOT / "tests" / "golden" / "plan_schema_digest.json").read_text())
+    _check(plan, schema)
+    assert plan["device"]["name"] == "b200" and plan["fusion"] == want
+    assert [t["name"] for t in plan["tensors"]] == [f"arg{i}" for i in range(len(shapes))]
+    assert plan["emission"]["fused_feasible"] is True
+    if shapes[0][0] == 32:
+        assert plan["emission"]["mapping"] == "stream-k-swap-ab"
+
+
+@pytest.mark.parametrize("doc,msg", [
+    ('{"tensors": [1, 2', "1:18"),
+    ('[]', "not an object"),
+    ('{"graph_id": "g"}', "tensors"),
+    ('{"tensors": [{"name": "arg0", "shape": [4, 8]}, {"name": "arg1", "shape": [9, 3]}], "fusion": "fused_mlp"}',
+     "fused_mlp needs"),
+    ('{"tensors": [{"name": "arg0", "shape": [4, 8]}, {"name": "arg1", "shape": [8, 3]}], "fusion": "bogus"}',
+     "unknown fusion"),
+    ('{"tensors": [{"name": "arg0", "shape": [4, 8.5]}]}', "not a non-negative integer"),
+])
+def test_tfb200_plan_rejects_bad_documents(doc, msg):
+    from tfb200 import _lib as L
+
+    rc, _, err = _plan(doc)
+    assert rc == L.TFB200_EINVAL and msg in err, err
+
+
 # Measured on B200 with CUDA events (bench.py): fused MLP 8192x4096x16384 1.678 ms
 # per step, fused RMSNorm+QKV 8192x4096x6144 0.339 ms, decode MLP 32x8192x28672
 # 0.183 ms per step.

@@ -49,6 +49,7 @@ EXPORTS = (
     "tfb200_device_status",
     "tfb200_clear_device_status",
     "tfb200_opt",
+    "tfb200_plan",
     "tfb200_selftest_bounded_wait",
     "tfb200_set_wait_limit_ns",
     "tfb200_launch_count",
@@ -116,6 +117,7 @@ def lib() -> ctypes.CDLL:
         "tfb200_device_status": ([], i32),
         "tfb200_clear_device_status": ([], i32),
         "tfb200_opt": ([ctypes.c_char_p, ctypes.c_char_p, vp, sz, ctypes.POINTER(ctypes.c_size_t)], i32),
+        "tfb200_plan": ([ctypes.c_char_p, vp, sz, ctypes.POINTER(ctypes.c_size_t)], i32),
         "tfb200_selftest_bounded_wait": ([u64, vp], i32),
         "tfb200_set_wait_limit_ns": ([u64], None),
         "tfb200_launch_count": ([], u64),
