@@ -16,7 +16,8 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parents[1]
 TOOL = ROOT / "tt-flow_b200" / "bin" / "tfb200-opt"
 SUPPORTED = {"--tensixflow-device=b200", "--tensixflow-fuse-rmsnorm-matmul", "--tensixflow-plan-noc-sharding",
-             "--tensixflow-allocate-circular-buffers", "--tensixflow-to-json", "-verify-diagnostics"}
+             "--tensixflow-allocate-circular-buffers", "--tensixflow-to-json", "-verify-diagnostics",
+             "--tensixflow-import-ttir", "--allow-unregistered-dialect"}
 
 
 def filecheck() -> str | None:
@@ -59,10 +60,13 @@ def run_file(path: Path) -> dict:
             if not tool_flags <= SUPPORTED:
                 res["skipped"].append(r)
                 continue
-            cmd = r.replace("%s", str(path)).replace("%t", str(t))
+            cmd = r.replace("%s", str(path)).replace("%t", str(t)).replace("%S", str(path.parent))
             cmd = re.sub(r"\btensixflow-opt\b", str(TOOL), cmd)
             cmd = re.sub(r"\bFileCheck\b", fc, cmd)
-            cmd = re.sub(r"^not\s+", "! ", cmd)
+            if re.match(r"^not\s+", cmd):
+                # lit's `not` inverts the status of its own command only, not the pipeline's
+                first, sep, rest = cmd.partition("|")
+                cmd = "( ! " + re.sub(r"^not\s+", "", first).strip() + " )" + (" |" + rest if sep else "")
             p = subprocess.run(["bash", "-o", "pipefail", "-c", cmd], capture_output=True, text=True,
                                env=dict(os.environ))
             res["ran"] += 1

@@ -23,12 +23,15 @@ import litrun
 ROOT = Path(__file__).resolve().parents[1]
 REF_TESTS = Path("/root/reference/test/Tensixflow")
 # Reference lit files whose RUN lines exercise what this backend implements
-# (parsing/printing, verifiers, fusion passes). plan_noc_sharding.mlir checks
-# n150 Tensix planner numbers, which the B200 planner replaces; the other files
-# test Tenstorrent lowering, TT-Metalium emission or TTIR import.
+# (parsing/printing, verifiers, fusion passes, bare-TTIR import). RUN lines with
+# flags this backend does not implement (--tensixflow-infer-tile-layout, the
+# Tensix tile layouts of the n150 family) are skipped by the runner.
+# plan_noc_sharding.mlir checks n150 Tensix planner numbers, which the B200
+# planner replaces; the other files test Tenstorrent lowering or TT-Metalium
+# emission.
 REF_FILES = ["attrs.mlir", "dialect_parse.mlir", "smoke.mlir", "ops.mlir", "matmul.mlir", "rmsnorm.mlir",
              "shape_inference.mlir", "fused_ops.mlir", "fuse_rmsnorm_matmul.mlir", "fuse_mlp.mlir",
-             "fusion_tracking.mlir"]
+             "fusion_tracking.mlir", "import_ttir.mlir", "import_ttir_negative.mlir"]
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -219,3 +222,17 @@ def test_time_model_tracks_measurement(lit):
     plan = json.loads(out)
     est_s = plan["perf"]["est_cycles"] / 1.965e9
     assert abs(est_s / MEASURED_S[lit] - 1.0) < 0.15, (est_s, MEASURED_S[lit])
+
+
+def test_lit_runner_not_inverts_only_the_tool(tmp_path):
+    """`not tool | FileCheck` must still fail when FileCheck fails: a wrong CHECK is reported."""
+    bad = tmp_path / "bad.mlir"
+    bad.write_text("// RUN: not tensixflow-opt --allow-unregistered-dialect --tensixflow-import-ttir %s 2>&1 | "
+                   "FileCheck %s\n// CHECK: this text is not in the diagnostic\n"
+                   "func.func @f(%arg0: tensor<?x4xbf16>) -> tensor<?x4xbf16> {\n  return %arg0 : tensor<?x4xbf16>\n}\n")
+    r = litrun.run_file(bad)
+    assert r["ran"] == 1 and len(r["failed"]) == 1
+    good = tmp_path / "good.mlir"
+    good.write_text(bad.read_text().replace("this text is not in the diagnostic", "has a dynamic shape"))
+    r = litrun.run_file(good)
+    assert r["ran"] == 1 and not r["failed"], r

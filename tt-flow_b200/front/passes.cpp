@@ -11,6 +11,7 @@
 //       (shared-memory rings and TMEM accumulators; AllocateCircularBuffersPass.cpp:63-104)
 //   --tensixflow-to-json               plan JSON instead of IR (tensixflow-translate.cpp:75-222)
 //   --tensixflow-device=<name>         device selection (DeviceSelection.cpp:26-49); b200 only
+//   --tensixflow-import-ttir           bare-tensor TTIR in (ttir_import.cpp)
 #include "passes.hpp"
 
 #include <cstdlib>
@@ -18,6 +19,7 @@
 
 #include "ir.hpp"
 #include "plan.hpp"
+#include "ttir_import.hpp"
 
 namespace tfb200::front {
 
@@ -297,12 +299,16 @@ PipelineResult run_pipeline(const std::string& text, const std::vector<std::stri
   PipelineResult res;
   std::string device = "b200";
   std::vector<std::string> passes;
-  bool to_json = false;
+  bool to_json = false, import_ttir_text = false;
   for (const std::string& a : args)
     if (a == "-verify-diagnostics" || a == "--verify-diagnostics") return verify_diagnostics(text);
   for (const std::string& a : args) {
     if (a.rfind("--tensixflow-device=", 0) == 0) {
       device = a.substr(20);
+    } else if (a == "--tensixflow-import-ttir") {
+      import_ttir_text = true;
+    } else if (a == "--allow-unregistered-dialect") {
+      // the TTIR source parses as generic operations either way
     } else if (a == "--tensixflow-to-json") {
       to_json = true;
     } else if (a == "--tensixflow-fuse-rmsnorm-matmul" || a == "--tensixflow-plan-noc-sharding" ||
@@ -318,7 +324,7 @@ PipelineResult run_pipeline(const std::string& text, const std::vector<std::stri
     return res;
   }
   std::string err;
-  auto m = parse_module(text, &err);
+  auto m = import_ttir_text ? import_ttir(text, &err) : parse_module(text, &err);
   if (!m) {
     res.diag = err;
     return res;
