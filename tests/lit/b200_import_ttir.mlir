@@ -12,7 +12,7 @@
 // IMPORT: %1 = tensixflow.matmul %0, %arg2 : tensor<8192x4096xbf16> x tensor<4096x6144xbf16> -> tensor<8192x6144xbf16>
 // IMPORT: tensixflow.return %1 : tensor<8192x6144xbf16>
 
-// PLAN: tensixflow.emission = #tensixflow.emission<mapping "persistent-cta-tiles", cores_used 148, max_tiles_per_core 11
+// PLAN: tensixflow.emission = #tensixflow.emission<mapping "persistent-cta-pair-tiles", cores_used 148, max_tiles_per_core 11
 // PLAN-SAME: fused_feasible true>
 // PLAN-SAME: fusion "fused_rmsnorm_matmul"
 // PLAN: tensixflow.fused_rmsnorm_matmul %arg0, %arg1, %arg2 {epsilon = 9.99999974E-6 : f32

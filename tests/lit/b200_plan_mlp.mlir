@@ -6,9 +6,9 @@
 // GELU and residual-add never reach HBM: matmul1 out and add1 out
 // (8192 x 16384 each) and matmul2 out (8192 x 4096), 603979776 bytes saved.
 
-// CHECK: tensixflow.emission = #tensixflow.emission<mapping "persistent-cta-tiles", cores_used 148, max_tiles_per_core 28, dram_read 738238464, dram_write 402685952, fused_stage_tiles 96, fused_feasible true>
+// CHECK: tensixflow.emission = #tensixflow.emission<mapping "persistent-cta-pair-tiles", cores_used 148, max_tiles_per_core 28, dram_read 738238464, dram_write 402685952, fused_stage_tiles 96, fused_feasible true>
 // CHECK-SAME: tensixflow.fusion_report = 1 : i64
-// CHECK-SAME: fusion "fused_mlp", cbs [0:4:16384, 1:4:32768, 16:2:131072]
+// CHECK-SAME: fusion "fused_mlp", cbs [0:6:16384, 1:6:16384, 16:2:131072]
 // CHECK-SAME: saved_read 603979776, saved_write 603979776, saved_intermediate 603979776>
 // CHECK: tensixflow.fused_mlp %arg0, %arg1, %arg2, %arg3, %arg4, %arg5 {epsilon = 1.0e-05 : f32, tensixflow.eliminated_bytes = 939524096 : i64, tensixflow.eliminated_tensors = 5 : i64}
 // CHECK-NOT: tensixflow.gelu

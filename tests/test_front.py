@@ -236,3 +236,59 @@ def test_lit_runner_not_inverts_only_the_tool(tmp_path):
     good.write_text(bad.read_text().replace("this text is not in the diagnostic", "has a dynamic shape"))
     r = litrun.run_file(good)
     assert r["ran"] == 1 and not r["failed"], r
+
+
+def _emit(tmp_path, lit, *extra):
+    out = tmp_path / "project"
+    text = (ROOT / "tests" / "lit" / lit).read_text()
+    rc, _, err = _opt(text, "--tensixflow-fuse-rmsnorm-matmul", *extra, f"--tensixflow-emit-cuda=output-dir={out}")
+    return rc, out, err
+
+
+@pytest.mark.parametrize("lit", ["b200_plan_mlp.mlir", "b200_plan_rmsnorm_matmul.mlir", "b200_plan_decode.mlir"])
+def test_emit_cuda_project_writes_a_buildable_project(tmp_path, lit):
+    rc, out, err = _emit(tmp_path, lit, "--tensixflow-plan-noc-sharding")
+    assert rc == 0, err
+    for f in ("host.cpp", "Makefile", "run.sh", "README.md", "plan.json"):
+        assert (out / f).stat().st_size > 0, f
+    host = (out / "host.cpp").read_text()
+    assert "TENSIXFLOW_RESULT" in host and "kPccThreshold" in host and "std::mt19937" in host
+    assert "tfb200_fused_" in host
+    assert "fused_feasible | true" in (out / "README.md").read_text()
+    assert json.loads((out / "plan.json").read_text())["emission"]["fused_feasible"] is True
+    assert 'TENSIXFLOW_RESULT {"status"' in (out / "run.sh").read_text()
+    # The host program compiles and links against the library without a GPU.
+    import shutil
+
+    if shutil.which("g++") and Path("/usr/local/cuda/include/cuda_runtime.h").exists():
+        r = subprocess.run(["make", "-s", "-C", str(out), "host", f"TFB200_ROOT={ROOT}"], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+        assert (out / "host").exists()
+
+
+def test_emit_cuda_refuses_an_unplanned_module(tmp_path):
+    rc, out, err = _emit(tmp_path, "b200_plan_mlp.mlir")
+    assert rc != 0 and "run --tensixflow-plan-noc-sharding before" in err
+    assert not out.exists()
+
+
+def test_emit_metalium_flag_names_the_cuda_project_for_b200(tmp_path):
+    out = tmp_path / "p2"
+    text = (ROOT / "tests" / "lit" / "b200_plan_rmsnorm_matmul.mlir").read_text()
+    rc, _, err = _opt(text, "--tensixflow-plan-noc-sharding", f"--tensixflow-emit-metalium=output-dir={out}")
+    assert rc == 0, err
+    assert (out / "host.cpp").exists()
+    rc, _, err = _opt(text, "--tensixflow-plan-noc-sharding", "--tensixflow-emit-cuda=dir=x")
+    assert rc != 0 and "expects output-dir=" in err
+
+
+def test_emit_cuda_refuses_an_infeasible_plan(tmp_path):
+    text = """tensixflow.func @dyn(%x: tensor<?x4096xbf16>, %gamma: tensor<4096xbf16>, %w: tensor<4096x6144xbf16>) -> tensor<?x6144xbf16> {
+  %0 = tensixflow.rmsnorm %x, %gamma {epsilon = 1.0e-05 : f32} : tensor<?x4096xbf16>, tensor<4096xbf16> -> tensor<?x4096xbf16>
+  %1 = tensixflow.matmul %0, %w : tensor<?x4096xbf16> x tensor<4096x6144xbf16> -> tensor<?x6144xbf16>
+  tensixflow.return %1 : tensor<?x6144xbf16>
+}"""
+    out = tmp_path / "never"
+    rc, _, err = _opt(text, "--tensixflow-plan-noc-sharding", f"--tensixflow-emit-cuda=output-dir={out}")
+    assert rc != 0 and "not fused_feasible" in err
+    assert not out.exists()

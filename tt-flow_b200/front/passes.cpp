@@ -12,12 +12,15 @@
 //   --tensixflow-to-json               plan JSON instead of IR (tensixflow-translate.cpp:75-222)
 //   --tensixflow-device=<name>         device selection (DeviceSelection.cpp:26-49); b200 only
 //   --tensixflow-import-ttir           bare-tensor TTIR in (ttir_import.cpp)
+//   --tensixflow-emit-cuda=output-dir=<dir>   standalone CUDA project (emit_cuda.cpp;
+//       --tensixflow-emit-metalium=output-dir=<dir> is read the same way for the B200)
 #include "passes.hpp"
 
 #include <cstdlib>
 #include <sstream>
 
 #include "ir.hpp"
+#include "emit_cuda.hpp"
 #include "plan.hpp"
 #include "ttir_import.hpp"
 
@@ -299,7 +302,8 @@ PipelineResult run_pipeline(const std::string& text, const std::vector<std::stri
   PipelineResult res;
   std::string device = "b200";
   std::vector<std::string> passes;
-  bool to_json = false, import_ttir_text = false;
+  bool to_json = false, import_ttir_text = false, emit = false;
+  std::string emit_dir;
   for (const std::string& a : args)
     if (a == "-verify-diagnostics" || a == "--verify-diagnostics") return verify_diagnostics(text);
   for (const std::string& a : args) {
@@ -309,6 +313,16 @@ PipelineResult run_pipeline(const std::string& text, const std::vector<std::stri
       import_ttir_text = true;
     } else if (a == "--allow-unregistered-dialect") {
       // the TTIR source parses as generic operations either way
+    } else if (a.rfind("--tensixflow-emit-cuda=", 0) == 0 || a.rfind("--tensixflow-emit-metalium=", 0) == 0) {
+      // The project of the selected device; for the B200 that is a CUDA project, so the reference's
+      // emission flag names it too.
+      const std::string opt = a.substr(a.find('=') + 1);
+      if (opt.rfind("output-dir=", 0) != 0) {
+        res.diag = "error: " + a.substr(0, a.find('=')) + " expects output-dir=<directory>";
+        return res;
+      }
+      emit_dir = opt.substr(11);
+      emit = true;
     } else if (a == "--tensixflow-to-json") {
       to_json = true;
     } else if (a == "--tensixflow-fuse-rmsnorm-matmul" || a == "--tensixflow-plan-noc-sharding" ||
@@ -364,6 +378,17 @@ PipelineResult run_pipeline(const std::string& text, const std::vector<std::stri
   if (!err.empty()) {
     res.diag = "error: " + err;
     return res;
+  }
+  if (emit) {
+    if (!planned) {
+      res.diag = "error: the module has no tensixflow.emission block; run --tensixflow-plan-noc-sharding before "
+                 "--tensixflow-emit-cuda";
+      return res;
+    }
+    if (!emit_cuda_project(*m, plan, emit_dir, &err)) {
+      res.diag += "error: " + err;
+      return res;
+    }
   }
   if (to_json) {
     if (!planned) {

@@ -13,8 +13,14 @@ namespace {
 int64_t cdiv(int64_t a, int64_t b) { return b > 0 ? (a + b - 1) / b : 0; }
 
 // Tile geometry of the kernels in libtfb200 (gemm_sm100.cu, stream_sm100.cu).
+// One CTA (k_gemm, up to 128 rows): 128 x 256 tiles, 4 stages.
 constexpr int64_t kTileM = 128, kTileN = 256, kTileK = 64, kStages = 4;
 constexpr int64_t kGemmCtlBytes = 112;   // mbarriers + TMEM address + abort flag
+// CTA pair (k_gemm_pair, more than 128 rows): 256 x 256 tiles per pair of CTAs
+// (cta_group::2), 6 stages of 16 KiB A + 16 KiB B per CTA, 8 KiB of epilogue
+// staging, at most 74 resident pairs.
+constexpr int64_t kPairTileM = 256, kPairStages = 6, kPairStagingBytes = 8192, kPairCtlBytes = 144;
+constexpr int64_t kMaxPairs = 74;
 constexpr int64_t kStreamCtlBytes = 244;
 constexpr int64_t kStreamMaxRows = 64;   // fused MLP switches to the streamed kernel at or below
 constexpr int64_t kStreamN = 128, kStreamK = 64, kStreamMaxStages = 12, kStreamBudget = 200 * 1024;
@@ -32,15 +38,17 @@ struct Gemm {
   int64_t M, N, K;
 };
 
-void add_tiled(B200Plan& p, const Gemm& g) {
+void add_tiled(B200Plan& p, const Gemm& g, bool pair) {
   const B200Device& d = b200();
-  const int64_t tiles = cdiv(g.M, kTileM) * cdiv(g.N, kTileN);
+  const int64_t tm = pair ? kPairTileM : kTileM;
+  const int64_t tiles = cdiv(g.M, tm) * cdiv(g.N, kTileN);
   p.tiles += tiles;
-  const int64_t ctas = std::min<int64_t>(d.sms(), tiles);
-  p.ctas = std::max(p.ctas, ctas);
-  p.max_tiles_per_cta = std::max(p.max_tiles_per_cta, cdiv(tiles, ctas));
+  // A pair's two CTAs share one tile; max_tiles_per_cta counts tiles per pair then.
+  const int64_t workers = std::min<int64_t>(pair ? kMaxPairs : d.sms(), tiles);
+  p.ctas = std::max(p.ctas, pair ? 2 * workers : workers);
+  p.max_tiles_per_cta = std::max(p.max_tiles_per_cta, cdiv(tiles, workers));
   // every staged A/B byte is written by TMA and read by the MMA once
-  p.l1_bytes += 2 * tiles * cdiv(g.K, kTileK) * (kTileM + kTileN) * kTileK * 2;
+  p.l1_bytes += 2 * tiles * cdiv(g.K, kTileK) * (tm + kTileN) * kTileK * 2;
   p.launches += 1;
 }
 
@@ -91,6 +99,27 @@ B200Plan plan_b200(const PlanRequest& r) {
     p.launches = 3;
     p.fused_feasible = p.smem_bytes <= d.smem_per_cta && p.tmem_columns <= d.tmem_columns && mpad <= 256;
     if (!p.fused_feasible) p.infeasible_reason = "streamed stages exceed shared memory or TMEM";
+  } else if (M > kTileM) {
+    // What the library launches for more than 128 rows: the CTA-pair kernel.
+    p.mapping = "persistent-cta-pair-tiles";
+    p.tile_m = kPairTileM;
+    p.tile_n = kTileN;
+    p.tile_k = kTileK;
+    p.stages = kPairStages;
+    const int64_t a_stage = kTileM * kTileK * 2, b_stage = (kTileN / 2) * kTileK * 2;  // per CTA
+    p.smem_bytes = 1024 + kPairStages * (a_stage + b_stage) + kPairStagingBytes + kPairCtlBytes;
+    p.tmem_columns = 2 * kTileN;  // double-buffered 128 x 256 fp32 accumulator per CTA
+    if (mlp) {
+      add_tiled(p, {M, H, K}, true);
+      add_tiled(p, {M, N, H}, true);
+    } else {
+      add_tiled(p, {M, N, K}, true);
+    }
+    if (rms) p.launches += 1;  // staging pass
+    p.fused_stage_tiles = kPairStages * (a_stage + b_stage) / 2048;
+    p.cbs = {{0, kPairStages, a_stage}, {1, kPairStages, b_stage}, {16, 2, kTileM * kTileN * 4}};
+    p.fused_feasible = p.smem_bytes <= d.smem_per_cta && p.tmem_columns <= d.tmem_columns;
+    if (!p.fused_feasible) p.infeasible_reason = "tile stages exceed shared memory or TMEM";
   } else {
     p.mapping = "persistent-cta-tiles";
     p.tile_m = kTileM;
@@ -100,10 +129,10 @@ B200Plan plan_b200(const PlanRequest& r) {
     p.smem_bytes = 1024 + kStages * (kTileM + kTileN) * kTileK * 2 + kGemmCtlBytes;
     p.tmem_columns = 2 * kTileN;  // double-buffered fp32 accumulator
     if (mlp) {
-      add_tiled(p, {M, H, K});
-      add_tiled(p, {M, N, H});
+      add_tiled(p, {M, H, K}, false);
+      add_tiled(p, {M, N, H}, false);
     } else {
-      add_tiled(p, {M, N, K});
+      add_tiled(p, {M, N, K}, false);
     }
     if (rms) p.launches += 1;  // staging pass
     p.fused_stage_tiles = kStages * (kTileM + kTileN) * kTileK * 2 / 2048;

@@ -57,7 +57,7 @@ struct PlanRequest {
 struct B200Plan {
   PlanRequest req;
   // kernel mapping
-  std::string mapping;  // "persistent-cta-tiles" | "stream-k-swap-ab"
+  std::string mapping;  // "persistent-cta-pair-tiles" | "persistent-cta-tiles" | "stream-k-swap-ab"
   int64_t tile_m = 0, tile_n = 0, tile_k = 0, stages = 0;
   int64_t tiles = 0, ctas = 0, max_tiles_per_cta = 0;
   int64_t smem_bytes = 0, tmem_columns = 0;
