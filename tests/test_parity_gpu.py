@@ -199,3 +199,49 @@ def test_mlp_full_size(ops, golden_vectors, name):
     g = O.fused_mlp(xs, f32(t["gamma"]), f32(t["w1"]), f32(t["b1"]), f32(t["w2"]), xs, 1e-5, "tanh")
     assert_parity(yt[rows], g, f"{name} tanh sampled rows")
     assert np.all(np.isfinite(y)) and np.all(np.isfinite(yt))
+
+
+def test_concurrent_calls_from_threads_on_separate_streams(ops):
+    """The C ABI is stream-ordered and thread-safe across distinct streams: four host threads run fused
+    RMSNorm+MatMul, fused MLP (tiled and streamed) and matmul at once, each on its own stream."""
+    import threading
+
+    cases = []
+    for i, (m, k, n) in enumerate([(300, 512, 640), (8, 1024, 1024), (1024, 256, 512), (64, 512, 768)]):
+        rng = np.random.default_rng(100 + i)
+        x = W.bf16_bits(rng.standard_normal((m, k), dtype=np.float32))
+        g = W.bf16_bits(0.5 + rng.random(k, dtype=np.float32))
+        w1 = W.bf16_bits(rng.standard_normal((k, n), dtype=np.float32) / np.float32(np.sqrt(k)))
+        b1 = W.bf16_bits(0.02 * rng.standard_normal(n, dtype=np.float32))
+        w2 = W.bf16_bits(rng.standard_normal((n, k), dtype=np.float32) / np.float32(np.sqrt(n)))
+        cases.append((x, g, w1, b1, w2))
+    results, errors = [None] * len(cases), []
+
+    def run(i):
+        try:
+            x, g, w1, b1, w2 = cases[i]
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                X, G, W1, B1, W2 = dev(x), dev(g), dev(w1), dev(b1), dev(w2)
+                for _ in range(5):
+                    if i % 2 == 0:
+                        y = ops.fused_rmsnorm_matmul(X, G, W1, 1e-5)
+                    else:
+                        y = ops.fused_mlp(X, G, W1, B1, W2, X, 1e-5, gelu="tanh")
+                s.synchronize()
+                results[i] = host(y)
+        except Exception as e:  # noqa: BLE001 - reported below
+            errors.append((i, repr(e)))
+
+    threads = [threading.Thread(target=run, args=(i,)) for i in range(len(cases))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    for i, (x, g, w1, b1, w2) in enumerate(cases):
+        if i % 2 == 0:
+            want = O.fused_rmsnorm_matmul(f32(x), f32(g), f32(w1), 1e-5)
+        else:
+            want = O.fused_mlp(f32(x), f32(g), f32(w1), f32(b1), f32(w2), f32(x), 1e-5, "tanh")
+        assert_parity(results[i], want, f"thread {i}")

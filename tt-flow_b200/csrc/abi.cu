@@ -100,16 +100,18 @@ int* device_status_ptr(std::string* err) {
 }
 
 int sm_count() {
-  static int counts[64] = {};
+  static std::atomic<int> counts[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return 148;
-  if (!counts[dev]) {
+  int c = counts[dev].load(std::memory_order_relaxed);
+  if (!c) {
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    counts[dev] = n > 0 ? n : 148;
+    c = n > 0 ? n : 148;
+    counts[dev].store(c, std::memory_order_relaxed);
   }
-  return counts[dev];
+  return c;
 }
 
 void set_last_error(const std::string& msg) { g_last_error = msg; }

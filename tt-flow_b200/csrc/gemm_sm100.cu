@@ -30,6 +30,7 @@
 // device status word, drains what it issued and returns.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
@@ -730,17 +731,22 @@ template <bool MANUAL>
 int launch(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int grid, cudaStream_t s,
            std::string* err) {
   auto kern = k_gemm<MANUAL>;
-  static bool attr_set[64] = {};
+  // Per-device first-call setup; calls may come from several host threads.
+  static std::mutex mu;
+  static std::atomic<bool> ready[64];
   int dev = 0;
   cudaGetDevice(&dev);
   const size_t smem = smem_bytes();
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) {
-      if (err) *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
-      return -3;
+  if (dev >= 0 && dev < 64 && !ready[dev].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ready[dev].load(std::memory_order_relaxed)) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (e != cudaSuccess) {
+        if (err) *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+        return -3;
+      }
+      ready[dev].store(true, std::memory_order_release);
     }
-    attr_set[dev] = true;
   }
   kern<<<grid, Roles<MANUAL>::kThreads, smem, s>>>(ta, tb, kp);
   cudaError_t e = cudaGetLastError();
@@ -754,7 +760,9 @@ int launch(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int 
 
 int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                 int pair_tiles, cudaStream_t s, std::string* err) {
-  static bool attr_set[64] = {};
+  // Per-device first-call setup; calls may come from several host threads.
+  static std::mutex mu;
+  static std::atomic<bool> ready[64];
   static int max_clusters[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -763,7 +771,9 @@ int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb,
     if (err) *err = "device index out of range";
     return -3;
   }
-  if (!attr_set[dev]) {
+  std::unique_lock<std::mutex> lock(mu, std::defer_lock);
+  if (!ready[dev].load(std::memory_order_acquire)) lock.lock();
+  if (!ready[dev].load(std::memory_order_relaxed)) {
     cudaError_t e =
         cudaFuncSetAttribute(k_gemm_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemm_pair, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
@@ -790,8 +800,9 @@ int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb,
       return -3;
     }
     max_clusters[dev] = n;
-    attr_set[dev] = true;
+    ready[dev].store(true, std::memory_order_release);
   }
+  if (lock.owns_lock()) lock.unlock();
   const int pairs = pair_tiles < max_clusters[dev] ? pair_tiles : max_clusters[dev];
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * pairs, 1, 1);

@@ -31,7 +31,9 @@
 // (tensixflow lib/tensixflow/Codegen/EmitCompute.cpp:331-558).
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdlib>
+#include <mutex>
 
 #include "internal.h"
 #include "sm100_ptx.cuh"
@@ -656,16 +658,21 @@ int run_stream(const StreamProblem& sp, cudaStream_t stream, std::string* err) {
   CUtensorMap tw{}, ta{};
   if (!make_map(&tw, sp.W, sp.K, sp.N, sp.ldw, SBK, err)) return -3;
   if (!make_map(&ta, sp.A, sp.M, sp.K, sp.lda, static_cast<uint32_t>(p.Mpad), err)) return -3;
-  static bool attr_set[64] = {};
+  // Per-device first-call setup; calls may come from several host threads.
+  static std::mutex mu;
+  static std::atomic<bool> ready[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) {
-      if (err) *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
-      return -3;
+  if (dev >= 0 && dev < 64 && !ready[dev].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ready[dev].load(std::memory_order_relaxed)) {
+      cudaError_t e = cudaFuncSetAttribute(k_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      if (e != cudaSuccess) {
+        if (err) *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+        return -3;
+      }
+      ready[dev].store(true, std::memory_order_release);
     }
-    attr_set[dev] = true;
   }
   const int grid = p.units < sm_count() ? p.units : sm_count();
   // Programmatic dependent launch: this grid's prologue and first ring of
