@@ -6,9 +6,12 @@
 //   down      y   = bf16(h @ W2 + residual)              (kStreamFinishDown)
 //
 // Tensor parallel over G GPUs (W1 split by columns, b1 alongside, W2 split by
-// rows): every GPU runs staging + up on its shard and the down-projection as a
-// kStreamPartial into an fp32 [M, N] buffer, the buffers are summed across GPUs
-// by one all-reduce, and tfb200_residual_add finishes y = bf16(sum + residual).
+// rows): every GPU runs staging + up on its shard, then either
+//   * the down-projection with the cross-GPU reduction in the same kernel
+//     (kStreamTpReduce, tfb200_fused_mlp_tp): each column block is summed on its
+//     owner GPU from the ranks' 16-byte pushes and written to every GPU, or
+//   * the down-projection as a kStreamPartial into an fp32 [M, N] buffer, one
+//     all-reduce across GPUs, and tfb200_residual_add: y = bf16(sum + residual).
 #include <string>
 
 #include "../../include/tfb200.h"
