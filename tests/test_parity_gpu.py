@@ -245,3 +245,52 @@ def test_concurrent_calls_from_threads_on_separate_streams(ops):
         else:
             want = O.fused_mlp(f32(x), f32(g), f32(w1), f32(b1), f32(w2), f32(x), 1e-5, "tanh")
         assert_parity(results[i], want, f"thread {i}")
+
+
+def _special_rows(m, k, seed):
+    """Rows the reference golden treats specially: all zeros (output from eps alone), one NaN, one inf (1/rms = 0,
+    inf * 0 = NaN), and large finite values (1e18: x^2 still fits fp32 at this K)."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    x[1] = 0.0
+    x[2, 5] = np.nan
+    x[3] = 1e18
+    x[4, 7] = np.inf
+    return W.bf16_bits(x)
+
+
+def _check_special(got, want, what):
+    assert np.array_equal(np.isnan(got), np.isnan(want)), f"{what}: NaN pattern differs"
+    assert np.array_equal(np.isinf(got), np.isinf(want)), f"{what}: inf pattern differs"
+    rows = [r for r in range(want.shape[0]) if np.isfinite(want[r]).all()]
+    assert parity(got[rows], want[rows])["ok"], f"{what}: {parity(got[rows], want[rows])}"
+
+
+@pytest.mark.parametrize("m", [6, 300])
+def test_fused_rmsnorm_matmul_special_rows(ops, m):
+    k, n = 256, 384
+    x = _special_rows(m, k, 11)
+    rng = np.random.default_rng(12)
+    g = W.bf16_bits(0.5 + rng.random(k, dtype=np.float32))
+    w = W.bf16_bits(rng.standard_normal((k, n), dtype=np.float32) / np.float32(16))
+    got = host(ops.fused_rmsnorm_matmul(dev(x), dev(g), dev(w), 1e-5))
+    with np.errstate(all="ignore"):
+        want = O.fused_rmsnorm_matmul(f32(x), f32(g), f32(w), 1e-5)
+    _check_special(got, want, f"rmsnorm_matmul m={m}")
+
+
+@pytest.mark.parametrize("m", [6, 300])
+def test_fused_mlp_special_rows(ops, m):
+    """Streamed (6 rows) and tiled (300 rows) MLP paths: NaN / inf rows stay NaN, zero and huge rows stay finite."""
+    k, h = 256, 512
+    x = _special_rows(m, k, 13)
+    rng = np.random.default_rng(14)
+    g = W.bf16_bits(0.5 + rng.random(k, dtype=np.float32))
+    w1 = W.bf16_bits(rng.standard_normal((k, h), dtype=np.float32) / np.float32(16))
+    b1 = W.bf16_bits(0.02 * rng.standard_normal(h, dtype=np.float32))
+    w2 = W.bf16_bits(rng.standard_normal((h, k), dtype=np.float32) / np.float32(np.sqrt(h)))
+    r = W.bf16_bits(rng.standard_normal((m, k), dtype=np.float32))
+    got = host(ops.fused_mlp(dev(x), dev(g), dev(w1), dev(b1), dev(w2), dev(r), 1e-5, gelu="tanh"))
+    with np.errstate(all="ignore"):
+        want = O.fused_mlp(f32(x), f32(g), f32(w1), f32(b1), f32(w2), f32(r), 1e-5, "tanh")
+    _check_special(got, want, f"mlp m={m}")
