@@ -58,6 +58,71 @@ def peaks():
 # ------------------------------------------------------------------ clock sampler
 
 
+class NvmlClockSampler:
+    """Reads the SM clock, power and active clock-event reasons through NVML every
+    `period_s` from a background thread, so that a timed region of a few tens of
+    milliseconds still gets many samples (nvidia-smi's loop samples every 100 ms at
+    best). Read-only: no GPU setting is touched."""
+
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
+
+    def __init__(self, gpu_id: str, period_s: float = 0.005):
+        import threading
+
+        import pynvml
+
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        try:
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(gpu_id)
+        except pynvml.NVMLError:
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(int(gpu_id) if gpu_id.isdigit() else 0)
+        self.sm_max = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+        get = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        self._reasons = get
+        self.rows: list[tuple[float, float, float, int]] = []
+        self.period = period_s
+        self.halt = threading.Event()
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+
+    def _run(self):
+        nv, h = self.nv, self.h
+        while not self.halt.is_set():
+            try:
+                self.rows.append((time.time(), float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                  nv.nvmlDeviceGetPowerUsage(h) / 1000.0, int(self._reasons(h))))
+            except nv.NVMLError:
+                pass
+            self.halt.wait(self.period)
+
+    def stop(self, t0: float, t1: float) -> dict | None:
+        self.halt.set()
+        self.thread.join(timeout=5)
+        try:
+            self.nv.nvmlShutdown()
+        except self.nv.NVMLError:
+            pass
+        inside = [r for r in self.rows if t0 <= r[0] <= t1]
+        if not inside:
+            return None
+        reasons = sorted({n for r in inside for n, bit in self.REASONS if r[3] & bit})
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": self.sm_max,
+                "power_w_max": max(r[2] for r in inside), "reasons": reasons, "samples": len(inside),
+                "window": "timed", "source": f"NVML every {self.period * 1e3:.0f} ms"}
+
+
+def make_clock_sampler(gpu_id: str | None):
+    if gpu_id is None:
+        return None
+    try:
+        return NvmlClockSampler(gpu_id)
+    except Exception:
+        return ClockSampler(gpu_id)
+
+
 class ClockSampler:
     FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -362,7 +427,7 @@ def run_ours(args) -> int:
         if world > 1:
             dist.barrier()
 
-    sampler = ClockSampler(gpu_id_for_smi(local)) if rank == 0 else None
+    sampler = make_clock_sampler(gpu_id_for_smi(local)) if rank == 0 else None
     for _ in range(args.warmup):
         step()
     barrier()

@@ -504,6 +504,11 @@ __global__ void __launch_bounds__(256, 1)
   cluster_sync();  // both CTAs' barriers exist before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
+  // Programmatic dependent launch: the next grid in the stream may place its CTAs
+  // as this grid's CTAs exit (its prologue overlaps this grid's tail); this grid
+  // touches no global memory before the preceding grid has completed.
+  grid_dep_launch();
+  grid_dep_wait();
 
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
@@ -582,18 +587,14 @@ __global__ void __launch_bounds__(256, 1)
             const uint64_t bd = sdesc_sw128(b0 + k * 2048, 8192, 1024);
             mma_bf16_pair(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
-          const uint32_t e = smem_u32(&ctl->empty[stage]);
-          mma_commit_pair(e);
-          mma_commit_pair(mapa_shared(e, 1));
+          mma_commit_pair_both(smem_u32(&ctl->empty[stage]), 0x3);
           if (++stage == PSTAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (ok) {
-          const uint32_t f = smem_u32(&ctl->tfull[acc]);
-          mma_commit_pair(f);
-          mma_commit_pair(mapa_shared(f, 1));
+          mma_commit_pair_both(smem_u32(&ctl->tfull[acc]), 0x3);
         }
       }
       mma_commit_pair(smem_u32(&ctl->drain));
@@ -809,13 +810,15 @@ int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb,
   cfg.blockDim = dim3(256, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_pair, ta, tb, tc, kp);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {

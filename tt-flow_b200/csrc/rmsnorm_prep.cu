@@ -29,6 +29,11 @@ __global__ void __launch_bounds__(kWarps * 32) k_rms_prep(const bf16* __restrict
                                                           const bf16* __restrict__ gamma, int M, int K, float eps,
                                                           bf16* __restrict__ a, int64_t lda,
                                                           float* __restrict__ inv) {
+  // Launched with programmatic serialization: wait for the preceding grid (which
+  // may still read `a` or write `x`), then let the GEMM that follows place its
+  // CTAs and run its prologue beside this pass's last CTAs.
+  grid_dep_wait();
+  grid_dep_launch();
   const int lane = threadIdx.x & 31;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5); row < M; row += stride) {
@@ -173,13 +178,19 @@ int run_rms_prep(const bf16* x, int64_t ldx, const bf16* gamma, int64_t M, int64
   }
   const int64_t blocks64 = (M + kWarps - 1) / kWarps;
   const int blocks = static_cast<int>(blocks64 < 65535 * 8 ? blocks64 : 65535 * 8);
-  if (vec)
-    k_rms_prep<true><<<blocks, kWarps * 32, 0, stream>>>(x, ldx, gamma, static_cast<int>(M), static_cast<int>(K),
-                                                         eps, a, lda, inv);
-  else
-    k_rms_prep<false><<<blocks, kWarps * 32, 0, stream>>>(x, ldx, gamma, static_cast<int>(M),
-                                                          static_cast<int>(K), eps, a, lda, inv);
-  const cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(blocks, 1, 1);
+  cfg.blockDim = dim3(kWarps * 32, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int Mi = static_cast<int>(M), Ki = static_cast<int>(K);
+  cudaError_t e = vec ? cudaLaunchKernelEx(&cfg, k_rms_prep<true>, x, ldx, gamma, Mi, Ki, eps, a, lda, inv)
+                      : cudaLaunchKernelEx(&cfg, k_rms_prep<false>, x, ldx, gamma, Mi, Ki, eps, a, lda, inv);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     if (err) *err = std::string("rmsnorm staging launch: ") + cudaGetErrorString(e);
     return -3;

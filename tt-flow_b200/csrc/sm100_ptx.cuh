@@ -250,6 +250,14 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
                : "memory");
 }
+// One commit that arrives on the barrier at shared offset `bar` in every CTA of
+// `cta_mask` (bit i = CTA rank i of the cluster): both CTAs of a pair with 0x3.
+// This signals barriers only; it moves no data.
+__device__ __forceinline__ void mma_commit_pair_both(uint32_t bar, uint16_t cta_mask) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+               ::"r"(bar), "h"(cta_mask)
+               : "memory");
+}
 
 // Each thread of the warp reads 32 consecutive fp32 columns of its TMEM lane.
 __device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, uint32_t (&r)[32]) {
