@@ -42,7 +42,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # ncu captures summarised in profiles/k_gemm_mlp_8192x4096x16384.md and
 # profiles/k_stream_decode_mlp_32x8192x28672.md.
 TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {
-    "mlp_8192x4096x16384": (445.885e6 + 254.470e6 + 1461.034e6 + 63.625e6) / 2,
+    "mlp_8192x4096x16384": (468.280e6 + 252.043e6 + 1513.107e6 + 62.263e6) / 2,
     "decode_mlp_32x8192x28672": (476.737e6 + 6.666e6 + 474.709e6 + 6.204e6) / 2,
 }
 

@@ -27,10 +27,11 @@ constexpr int64_t kStreamN = 128, kStreamK = 64, kStreamMaxStages = 12, kStreamB
 constexpr double kLaunchSeconds = 3e-6;  // per kernel launch boundary (ramp up / drain)
 // Fractions of the measured peaks the kernels sustain, measured on B200 with
 // CUDA events: the tcgen05 GEMM ran the fused MLP 8192x4096x16384 at
-// 1310.7 TFLOP/s (80.1 % of 1635.3), the weight-streaming kernels the decode MLP
-// 32x8192x28672 at 5127 GB/s (78.5 % of 6534.5).
-constexpr double kTensorEfficiency = 0.80;
-constexpr double kHbmEfficiency = 0.785;
+// 1428-1466 TFLOP/s (87-90 % of 1635.3) and the fused RMSNorm+MatMul
+// 8192x4096x6144 at 1398 TFLOP/s (85.5 %); the weight-streaming kernels ran the
+// decode MLP 32x8192x28672 at 5262-5331 GB/s (80.5-81.6 % of 6534.5).
+constexpr double kTensorEfficiency = 0.87;
+constexpr double kHbmEfficiency = 0.81;
 
 std::string q(const std::string& s) { return "\"" + s + "\""; }
 
