@@ -90,6 +90,9 @@ __global__ void __launch_bounds__(kRowThreads) k_rms_prep_rows(const bf16* __res
                                                                float eps, bf16* __restrict__ a, int64_t lda,
                                                                float* __restrict__ inv, uint4* __restrict__ zero,
                                                                int64_t zero_vecs) {
+  // Launched with programmatic serialization, like k_rms_prep.
+  grid_dep_wait();
+  grid_dep_launch();
   if (blockIdx.x >= M) {
     const int64_t stride = static_cast<int64_t>(gridDim.x - M) * kRowThreads;
     for (int64_t i = static_cast<int64_t>(blockIdx.x - M) * kRowThreads + threadIdx.x; i < zero_vecs; i += stride)
@@ -159,9 +162,18 @@ int run_rms_prep(const bf16* x, int64_t ldx, const bf16* gamma, int64_t M, int64
     const int64_t zvec = static_cast<int64_t>(zero_bytes / 16);
     const int zblocks = zvec ? static_cast<int>(zvec / (kRowThreads * 8) + 1 < 512 ? zvec / (kRowThreads * 8) + 1 : 512)
                              : 0;
-    k_rms_prep_rows<<<static_cast<int>(M) + zblocks, kRowThreads, 0, stream>>>(
-        x, ldx, gamma, static_cast<int>(M), static_cast<int>(K), eps, a, lda, inv, static_cast<uint4*>(zero), zvec);
-    const cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(M) + static_cast<unsigned>(zblocks), 1, 1);
+    cfg.blockDim = dim3(kRowThreads, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_rms_prep_rows, x, ldx, gamma, static_cast<int>(M), static_cast<int>(K),
+                                       eps, a, lda, inv, static_cast<uint4*>(zero), zvec);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
       if (err) *err = std::string("rmsnorm staging launch: ") + cudaGetErrorString(e);
       return -3;

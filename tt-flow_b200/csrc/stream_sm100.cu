@@ -23,7 +23,7 @@
 // first ring of weight tiles overlap the preceding grid's tail.
 //
 // Warp roles: warp 0 TMA producer (W tile 64k x 128n as two 64-column boxes,
-// A tile Mpad x 64k), warp 1 MMA issuer (tcgen05.mma 128 x Mpad x 16, two TMEM
+// A tile Mpad x 64k), warp 1 MMA issuer (tcgen05.mma 128 x Mpad x 16, kAcc TMEM
 // accumulators), warp 2 TMEM allocator, warps 4-7 partial-sum and finishing
 // epilogue. All waits are bounded (kDevTimeout in the status word).
 //
@@ -67,11 +67,15 @@ struct SParams {
   TpPeers tp;
 };
 
+// TMEM accumulators in rotation: the MMA may run kAcc-1 segments ahead of the
+// epilogue.
+constexpr int kAcc = 4;
+
 struct SCtl {
   uint64_t full[kMaxStages];
   uint64_t empty[kMaxStages];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
+  uint64_t tfull[kAcc];
+  uint64_t tempty[kAcc];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -347,7 +351,7 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(smem_u32(&ctl->full[s]), 1);
       mbar_init(smem_u32(&ctl->empty[s]), 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kAcc; ++b) {
       mbar_init(smem_u32(&ctl->tfull[b]), 1);
       mbar_init(smem_u32(&ctl->tempty[b]), 128);
     }
@@ -446,8 +450,8 @@ __global__ void __launch_bounds__(256, 1)
         int64_t s0, e0;
         int nb;
         seg_range(segs, si, &s0, &e0, &nb);
-        const int acc = si & 1;
-        const uint32_t use = static_cast<uint32_t>(si >> 1);
+        const int acc = si % kAcc;
+        const uint32_t use = static_cast<uint32_t>(si / kAcc);
         if (!mbar_wait(smem_u32(&ctl->tempty[acc]), (use & 1u) ^ 1u, &ctl->abort, p.timeout_ns)) {
           raise_abort(ctl, p.status);
           ok = false;
@@ -493,8 +497,8 @@ __global__ void __launch_bounds__(256, 1)
       int64_t s0, e0;
       int nb;
       seg_range(segs, si, &s0, &e0, &nb);
-      const int acc = si & 1;
-      const uint32_t use = static_cast<uint32_t>(si >> 1);
+      const int acc = si % kAcc;
+      const uint32_t use = static_cast<uint32_t>(si / kAcc);
       // What a finisher of this column block reads besides the accumulator,
       // loaded while the block's MMAs run.
       const int nf = nb * SBN + et;
@@ -651,7 +655,7 @@ int run_stream(const StreamProblem& sp, cudaStream_t stream, std::string* err) {
   int stages = static_cast<int>(budget / (W_STAGE + a_stage));
   p.stages = stages > kMaxStages ? kMaxStages : stages;
   uint32_t cols = 32;
-  while (cols < static_cast<uint32_t>(2 * p.Mpad)) cols <<= 1;
+  while (cols < static_cast<uint32_t>(kAcc * p.Mpad)) cols <<= 1;
   p.tmem_cols = cols;
   const size_t smem = 1024 + static_cast<size_t>(p.stages) * (W_STAGE + a_stage) + sizeof(SCtl);
 
