@@ -836,21 +836,19 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // 256-row pair tile.
 // Stores through shared memory and TMA unless TFB200_GEMM_STORE=direct.
 bool tma_store_enabled() {
-  static int mode = -1;
-  if (mode < 0) {
+  static const bool on = [] {  // initialised once, thread-safe
     const char* v = std::getenv("TFB200_GEMM_STORE");
-    mode = (v && std::string(v) == "direct") ? 0 : 1;
-  }
-  return mode == 1;
+    return !(v && std::string(v) == "direct");
+  }();
+  return on;
 }
 
 bool use_pair(int64_t M) {
-  static int mode = -1;
-  if (mode < 0) {
+  static const bool pair = [] {  // initialised once, thread-safe
     const char* v = std::getenv("TFB200_GEMM_KERNEL");
-    mode = (v && std::string(v) == "single") ? 0 : 1;
-  }
-  return mode == 1 && M > BM;
+    return !(v && std::string(v) == "single");
+  }();
+  return pair && M > BM;
 }
 
 }  // namespace
