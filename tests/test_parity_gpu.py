@@ -81,7 +81,11 @@ def test_mlp_block_small(ops, golden_vectors, gelu):
     assert_parity(y, g, f"mlp_block_small/{gelu}")
 
 
-RAGGED = [(1, 64, 8), (200, 136, 300), (129, 64, 257), (300, 520, 40), (64, 4096, 1000), (70, 60, 33), (5, 7, 3)]
+# Above 1024 rows the staging pass holds each row in registers for K <= 4096
+# (K = 1000: lanes with 3 and 4 of the row's 125 16-byte chunks; K = 4096: 16 each)
+# and streams it twice above that (K = 4104).
+RAGGED = [(1, 64, 8), (200, 136, 300), (129, 64, 257), (300, 520, 40), (64, 4096, 1000), (70, 60, 33), (5, 7, 3),
+          (1100, 1000, 264), (2048, 4096, 256), (1030, 4104, 128)]
 
 
 @pytest.mark.parametrize("m,k,n", RAGGED)

@@ -80,6 +80,56 @@ __global__ void __launch_bounds__(kWarps * 32) k_rms_prep(const bf16* __restrict
   }
 }
 
+// Rows of up to kRegChunks * 32 * 8 elements (K <= 4096): the warp holds its
+// row in registers, so x is read from HBM once and all of a lane's 16-byte loads
+// are in flight together. Same arithmetic and summation order as k_rms_prep.
+constexpr int kRegChunks = 16;
+
+__global__ void __launch_bounds__(kWarps * 32) k_rms_prep_reg(const bf16* __restrict__ x, int64_t ldx,
+                                                              const bf16* __restrict__ gamma, int M, int K, float eps,
+                                                              bf16* __restrict__ a, int64_t lda,
+                                                              float* __restrict__ inv) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int lane = threadIdx.x & 31;
+  const int nchunk = K / 8;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5); row < M; row += stride) {
+    const uint4* xv = reinterpret_cast<const uint4*>(x + row * ldx);
+    uint4 v[kRegChunks];
+#pragma unroll
+    for (int i = 0; i < kRegChunks; ++i) {
+      const int c = lane + 32 * i;
+      v[i] = c < nchunk ? __ldg(xv + c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    uint64_t ss2 = 0;
+#pragma unroll
+    for (int i = 0; i < kRegChunks; ++i) {
+      if (lane + 32 * i < nchunk) {
+        ss2 = sq_acc_bf16x2(ss2, v[i].x);
+        ss2 = sq_acc_bf16x2(ss2, v[i].y);
+        ss2 = sq_acc_bf16x2(ss2, v[i].z);
+        ss2 = sq_acc_bf16x2(ss2, v[i].w);
+      }
+    }
+    float ss = __uint_as_float(static_cast<uint32_t>(ss2)) + __uint_as_float(static_cast<uint32_t>(ss2 >> 32));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) inv[row] = 1.0f / sqrtf(ss / static_cast<float>(K) + eps);
+    const uint4* gv = reinterpret_cast<const uint4*>(gamma);
+    uint4* av = reinterpret_cast<uint4*>(a + row * lda);
+#pragma unroll
+    for (int i = 0; i < kRegChunks; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nchunk) {
+        const uint4 g = __ldg(gv + c);
+        av[c] = make_uint4(mul_bf16x2(v[i].x, g.x), mul_bf16x2(v[i].y, g.y), mul_bf16x2(v[i].z, g.z),
+                           mul_bf16x2(v[i].w, g.w));
+      }
+    }
+  }
+}
+
 // Few rows: a whole CTA per row so the row's loads are all in flight at once,
 // and CTAs past the last row clear `zero` (the streamed GEMMs' fp32
 // accumulators and counters) with 16-byte stores.
@@ -200,8 +250,10 @@ int run_rms_prep(const bf16* x, int64_t ldx, const bf16* gamma, int64_t M, int64
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const int Mi = static_cast<int>(M), Ki = static_cast<int>(K);
-  cudaError_t e = vec ? cudaLaunchKernelEx(&cfg, k_rms_prep<true>, x, ldx, gamma, Mi, Ki, eps, a, lda, inv)
-                      : cudaLaunchKernelEx(&cfg, k_rms_prep<false>, x, ldx, gamma, Mi, Ki, eps, a, lda, inv);
+  cudaError_t e = vec && K <= kRegChunks * 32 * 8
+                      ? cudaLaunchKernelEx(&cfg, k_rms_prep_reg, x, ldx, gamma, Mi, Ki, eps, a, lda, inv)
+                  : vec ? cudaLaunchKernelEx(&cfg, k_rms_prep<true>, x, ldx, gamma, Mi, Ki, eps, a, lda, inv)
+                        : cudaLaunchKernelEx(&cfg, k_rms_prep<false>, x, ldx, gamma, Mi, Ki, eps, a, lda, inv);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     if (err) *err = std::string("rmsnorm staging launch: ") + cudaGetErrorString(e);
