@@ -9,7 +9,7 @@
 // 64-column TMEM double buffer fit; the model is HBM-bound.
 
 // CHECK: tensixflow.emission = #tensixflow.emission<mapping "stream-k-swap-ab", cores_used 148, max_tiles_per_core 388, dram_read 943005696, dram_write 2883712, fused_stage_tiles 100, fused_feasible true>
-// CHECK-SAME: weight "shard", storage "HBM", fusion "fused_mlp", cbs [0:10:4096, 1:10:16384, 16:2:16384]
+// CHECK-SAME: weight "shard", storage "HBM", fusion "fused_mlp", cbs [0:10:4096, 1:10:16384, 16:4:16384]
 // JSON: "graph_id": "decode"
 // JSON: "weight_strategy": "shard"
 // JSON: "mapping": "stream-k-swap-ab"

@@ -17,13 +17,14 @@ int64_t cdiv(int64_t a, int64_t b) { return b > 0 ? (a + b - 1) / b : 0; }
 constexpr int64_t kTileM = 128, kTileN = 256, kTileK = 64, kStages = 4;
 constexpr int64_t kGemmCtlBytes = 112;   // mbarriers + TMEM address + abort flag
 // CTA pair (k_gemm_pair, more than 128 rows): 256 x 256 tiles per pair of CTAs
-// (cta_group::2), 6 stages of 16 KiB A + 16 KiB B per CTA, 8 KiB of epilogue
-// staging, at most 74 resident pairs.
-constexpr int64_t kPairTileM = 256, kPairStages = 6, kPairStagingBytes = 8192, kPairCtlBytes = 144;
+// (cta_group::2), 6 stages of 16 KiB A + 16 KiB B per CTA, 16 KiB of epilogue
+// staging (two 32 x 32 bf16 buffers per epilogue warp), at most 74 resident pairs.
+constexpr int64_t kPairTileM = 256, kPairStages = 6, kPairStagingBytes = 16384, kPairCtlBytes = 144;
 constexpr int64_t kMaxPairs = 74;
-constexpr int64_t kStreamCtlBytes = 244;
+constexpr int64_t kStreamCtlBytes = 276;
 constexpr int64_t kStreamMaxRows = 64;   // fused MLP switches to the streamed kernel at or below
 constexpr int64_t kStreamN = 128, kStreamK = 64, kStreamMaxStages = 12, kStreamBudget = 200 * 1024;
+constexpr int64_t kStreamAcc = 4;  // TMEM accumulators of the streamed kernel, in rotation
 constexpr double kLaunchSeconds = 3e-6;  // per kernel launch boundary (ramp up / drain)
 // Fractions of the measured peaks the kernels sustain, measured on B200 with
 // CUDA events: the tcgen05 GEMM ran the fused MLP 8192x4096x16384 at
@@ -85,7 +86,7 @@ B200Plan plan_b200(const PlanRequest& r) {
     p.stages = std::min<int64_t>(kStreamMaxStages, kStreamBudget / (w_stage + a_stage));
     p.smem_bytes = 1024 + p.stages * (w_stage + a_stage) + kStreamCtlBytes;
     int64_t cols = 32;
-    while (cols < 2 * mpad) cols <<= 1;
+    while (cols < kStreamAcc * mpad) cols <<= 1;
     p.tmem_columns = cols;
     const int64_t units_up = cdiv(H, kStreamN) * cdiv(K, kStreamK);
     const int64_t units_dn = cdiv(N, kStreamN) * cdiv(H, kStreamK);
@@ -96,7 +97,7 @@ B200Plan plan_b200(const PlanRequest& r) {
     p.l1_bytes = 2 * (units_up + units_dn) * (w_stage + a_stage);
     p.fused_stage_tiles = p.stages * (w_stage + a_stage) / 2048;
     p.weight = "shard";  // every CTA streams a disjoint slice of the weights
-    p.cbs = {{0, p.stages, a_stage}, {1, p.stages, w_stage}, {16, 2, mpad * 128 * 4}};
+    p.cbs = {{0, p.stages, a_stage}, {1, p.stages, w_stage}, {16, kStreamAcc, mpad * 128 * 4}};
     p.launches = 3;
     p.fused_feasible = p.smem_bytes <= d.smem_per_cta && p.tmem_columns <= d.tmem_columns && mpad <= 256;
     if (!p.fused_feasible) p.infeasible_reason = "streamed stages exceed shared memory or TMEM";
