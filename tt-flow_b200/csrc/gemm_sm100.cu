@@ -116,10 +116,43 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, SmemCtl
   return ok;
 }
 
+// GELU (tanh form) on an fp32 pair: with c1 = sqrt(2/pi) and c2 = c1 * 0.044715,
+// u = x * (c1 + c2 * x^2) and gelu = h + h * tanh(u) with h = x / 2: three
+// packed ops for u, two for the result, tanh per element.
+__device__ __forceinline__ uint64_t gelu_tanh2(uint64_t x) {
+  const uint64_t c1 = f2(0.7978845608028654f, 0.7978845608028654f);
+  const uint64_t c2 = f2(0.035677408136300125f, 0.035677408136300125f);
+  const uint64_t half = f2(0.5f, 0.5f);
+  const uint64_t u = f2_mul(x, f2_fma(f2_mul(x, x), c2, c1));
+  float u0, u1;
+  f2_split(u, u0, u1);
+  const uint64_t t = f2(tanh_approx(u0), tanh_approx(u1));
+  const uint64_t h = f2_mul(x, half);
+  return f2_fma(h, t, h);
+}
+
 // Row scale, bias, GELU and residual on 32 accumulator columns of one row
 // (columns col0 .. col0+31 of `row`), in fp32.
 __device__ __forceinline__ void epilogue_values(const KParams& p, const uint32_t (&v)[32], float scale, int64_t row,
                                                 int col0, float (&f)[32]) {
+  if (p.vec_ok && col0 + 32 <= p.N && p.gelu == kGeluTanh && p.bias && !p.residual) {
+    // The MLP up-projection's epilogue on fp32 pairs: scale, bias, GELU.
+    const uint64_t s2 = f2(scale, scale);
+    const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint4 b = __ldg(bp + u);
+      const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j = u * 8 + 2 * e;
+        uint64_t x = f2_mul(f2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])), s2);
+        x = gelu_tanh2(f2_add(x, f2_from_bf16x2(bw[e])));
+        f2_split(x, f[j], f[j + 1]);
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * scale;
   const bool full = p.vec_ok && (col0 + 32 <= p.N);

@@ -322,6 +322,36 @@ __device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
   return r;
 }
 
+// Packed pairs of fp32 (lo in bits 0-31): sm_100 executes one f32x2 add, mul or
+// fma for both halves, each rounded to nearest even as the scalar op would be.
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+// The two bf16 values of a bf16x2 word as an fp32 pair (exact).
+__device__ __forceinline__ uint64_t f2_from_bf16x2(uint32_t w) {
+  return (static_cast<uint64_t>(w & 0xFFFF0000u) << 32) | static_cast<uint64_t>(w << 16);
+}
+
 // acc (two packed fp32 sums) += (lo(x)^2, hi(x)^2) for a bf16x2 word x.
 __device__ __forceinline__ uint64_t sq_acc_bf16x2(uint64_t acc, uint32_t x) {
   const uint64_t xx = (static_cast<uint64_t>(x & 0xFFFF0000u) << 32) | static_cast<uint64_t>(x << 16);

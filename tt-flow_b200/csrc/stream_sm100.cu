@@ -551,18 +551,19 @@ __global__ void __launch_bounds__(256, 1)
       }
       if (ctl->finisher) {
         if (nf < p.N) {
-          // Sixteen rows per step so their loads are in flight together.
+          // Thirty-two rows per step so their loads are in flight together (one
+          // L2 round trip for up to 32 tokens).
 #pragma unroll
-          for (int m0 = 0; m0 < kStreamMaxRows; m0 += 16) {
+          for (int m0 = 0; m0 < kStreamMaxRows; m0 += 32) {
             if (m0 >= p.M) break;
-            float val[16];
+            float val[32];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
+            for (int j = 0; j < 32; ++j) {
               const int m = m0 + j;
               val[j] = m < p.M ? __ldcg(p.acc + static_cast<int64_t>(m) * p.N + nf) : 0.0f;
             }
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
+            for (int j = 0; j < 32; ++j) {
               const int m = m0 + j;
               if (m >= p.M) break;
               float v = val[j];
