@@ -37,20 +37,21 @@
 #include <string>
 
 #include "internal.h"
+#include "kernel_config.h"
 #include "sm100_ptx.cuh"
 
 namespace tfb200 {
 
 namespace {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int BK = 64;
-constexpr int STAGES = 4;
+constexpr int BM = cfg::kTileM;
+constexpr int BN = cfg::kTileN;
+constexpr int BK = cfg::kTileK;
+constexpr int STAGES = cfg::kStages;
 constexpr uint32_t A_STAGE_BYTES = BM * BK * 2;  // 16 KiB
 constexpr uint32_t B_STAGE_BYTES = BN * BK * 2;  // 32 KiB
 constexpr uint32_t TMEM_COLS = 2 * BN;           // two accumulators
-constexpr int GROUP_M = 16;                      // raster group (tiles of M)
+constexpr int GROUP_M = cfg::kGroupM;            // raster group (tiles of M)
 
 struct KParams {
   int M, N, K;
@@ -80,6 +81,8 @@ struct SmemCtl {
   uint32_t tmem_base;
   int abort;
 };
+
+static_assert(sizeof(SmemCtl) == cfg::kGemmCtlBytes, "planner's control-block size");
 
 constexpr size_t smem_bytes() {
   return 1024 /*alignment slack*/ + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + sizeof(SmemCtl);
@@ -470,7 +473,7 @@ __global__ void __launch_bounds__(Roles<MANUAL>::kThreads, 1)
 // by the leader with both CTAs' bytes); the leader's MMA thread signals each
 // CTA's `empty` and `tfull` barrier; both CTAs' epilogue warps arrive on the
 // leader's `tempty` barrier. Every wait is bounded.
-constexpr int PSTAGES = 6;
+constexpr int PSTAGES = cfg::kPairStages;
 constexpr int PBM = 2 * BM;                       // rows per pair tile
 constexpr uint32_t PB_STAGE_BYTES = BM * BK * 2;  // this CTA's 128 of the 256 B columns
 
@@ -487,6 +490,9 @@ struct PairCtl {
 // Epilogue staging for TMA stores: per epilogue warp two 32 x 32 bf16 buffers.
 constexpr uint32_t C_STAGE_BYTES = 32 * 32 * 2;
 constexpr uint32_t C_STAGING_BYTES = 4 * 2 * C_STAGE_BYTES;
+static_assert(C_STAGING_BYTES == cfg::kPairStagingBytes, "planner's epilogue staging size");
+static_assert(sizeof(PairCtl) == cfg::kPairCtlBytes, "planner's pair control-block size");
+static_assert(PBM == cfg::kPairTileM, "planner's pair tile");
 
 constexpr size_t pair_smem_bytes() {
   return 1024 + PSTAGES * (A_STAGE_BYTES + PB_STAGE_BYTES) + C_STAGING_BYTES + sizeof(PairCtl);

@@ -8,6 +8,8 @@
 #include <cstdint>
 #include <string>
 
+#include "kernel_config.h"
+
 namespace tfb200 {
 
 using bf16 = __nv_bfloat16;
@@ -90,7 +92,7 @@ int stream_mpad(int64_t m);
 size_t stream_counter_bytes(int64_t n);
 
 // Streamed (decode-shaped) fused MLP, decode.cu. Used for M <= kStreamMaxRows.
-constexpr int64_t kStreamMaxRows = 64;
+constexpr int64_t kStreamMaxRows = cfg::kStreamMaxRows;
 size_t decode_core_bytes(int64_t m, int64_t k, int64_t h, int64_t n);
 size_t decode_mlp_bytes(int64_t m, int64_t k, int64_t h, int64_t n);
 bool decode_eligible(int64_t m, const void* w1, int64_t ldw1, const void* w2, int64_t ldw2);

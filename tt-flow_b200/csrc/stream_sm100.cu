@@ -36,16 +36,17 @@
 #include <mutex>
 
 #include "internal.h"
+#include "kernel_config.h"
 #include "sm100_ptx.cuh"
 
 namespace tfb200 {
 
 namespace {
 
-constexpr int SBN = 128;  // output features per unit (MMA M)
-constexpr int SBK = 64;   // k per unit
+constexpr int SBN = cfg::kStreamN;  // output features per unit (MMA M)
+constexpr int SBK = cfg::kStreamK;  // k per unit
 constexpr uint32_t W_STAGE = SBN * SBK * 2;  // 16 KiB
-constexpr int kMaxStages = 12;
+constexpr int kMaxStages = cfg::kStreamMaxStages;
 
 struct SParams {
   int M, N, K, Mpad;
@@ -69,7 +70,7 @@ struct SParams {
 
 // TMEM accumulators in rotation: the MMA may run kAcc-1 segments ahead of the
 // epilogue.
-constexpr int kAcc = 4;
+constexpr int kAcc = cfg::kStreamAcc;
 
 struct SCtl {
   uint64_t full[kMaxStages];
@@ -81,6 +82,8 @@ struct SCtl {
   int abort;
   int finisher;
 };
+
+static_assert(sizeof(SCtl) == cfg::kStreamCtlBytes, "planner's control-block size");
 
 __device__ __forceinline__ int64_t unit_start(int c, int units, int grid) {
   return static_cast<int64_t>(c) * units / grid;
@@ -652,7 +655,7 @@ int run_stream(const StreamProblem& sp, cudaStream_t stream, std::string* err) {
   p.status = status;
   p.timeout_ns = wait_limit_ns();
   const uint32_t a_stage = static_cast<uint32_t>(p.Mpad) * SBK * 2;
-  const size_t budget = 200 * 1024;
+  const size_t budget = cfg::kStreamBudget;
   int stages = static_cast<int>(budget / (W_STAGE + a_stage));
   p.stages = stages > kMaxStages ? kMaxStages : stages;
   uint32_t cols = 32;

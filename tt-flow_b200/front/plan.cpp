@@ -1,6 +1,8 @@
 // B200 planner, roofline model and plan JSON (see plan.hpp).
 #include "plan.hpp"
 
+#include "../csrc/kernel_config.h"
+
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
@@ -12,19 +14,19 @@ namespace {
 
 int64_t cdiv(int64_t a, int64_t b) { return b > 0 ? (a + b - 1) / b : 0; }
 
-// Tile geometry of the kernels in libtfb200 (gemm_sm100.cu, stream_sm100.cu).
-// One CTA (k_gemm, up to 128 rows): 128 x 256 tiles, 4 stages.
-constexpr int64_t kTileM = 128, kTileN = 256, kTileK = 64, kStages = 4;
-constexpr int64_t kGemmCtlBytes = 112;   // mbarriers + TMEM address + abort flag
-// CTA pair (k_gemm_pair, more than 128 rows): 256 x 256 tiles per pair of CTAs
-// (cta_group::2), 6 stages of 16 KiB A + 16 KiB B per CTA, 16 KiB of epilogue
-// staging (two 32 x 32 bf16 buffers per epilogue warp), at most 74 resident pairs.
-constexpr int64_t kPairTileM = 256, kPairStages = 6, kPairStagingBytes = 16384, kPairCtlBytes = 144;
+// Tile geometry of the kernels in libtfb200, from the header the kernels use
+// (csrc/kernel_config.h): one CTA (k_gemm, up to 128 rows), the CTA pair
+// (k_gemm_pair, more than 128 rows; at most 74 resident pairs) and the
+// weight-streaming kernel (k_stream, at most kStreamMaxRows rows).
+constexpr int64_t kTileM = cfg::kTileM, kTileN = cfg::kTileN, kTileK = cfg::kTileK, kStages = cfg::kStages;
+constexpr int64_t kGemmCtlBytes = cfg::kGemmCtlBytes;
+constexpr int64_t kPairTileM = cfg::kPairTileM, kPairStages = cfg::kPairStages;
+constexpr int64_t kPairStagingBytes = cfg::kPairStagingBytes, kPairCtlBytes = cfg::kPairCtlBytes;
 constexpr int64_t kMaxPairs = 74;
-constexpr int64_t kStreamCtlBytes = 276;
-constexpr int64_t kStreamMaxRows = 64;   // fused MLP switches to the streamed kernel at or below
-constexpr int64_t kStreamN = 128, kStreamK = 64, kStreamMaxStages = 12, kStreamBudget = 200 * 1024;
-constexpr int64_t kStreamAcc = 4;  // TMEM accumulators of the streamed kernel, in rotation
+constexpr int64_t kStreamCtlBytes = cfg::kStreamCtlBytes;
+constexpr int64_t kStreamMaxRows = cfg::kStreamMaxRows;
+constexpr int64_t kStreamN = cfg::kStreamN, kStreamK = cfg::kStreamK, kStreamMaxStages = cfg::kStreamMaxStages;
+constexpr int64_t kStreamBudget = cfg::kStreamBudget, kStreamAcc = cfg::kStreamAcc;
 constexpr double kLaunchSeconds = 3e-6;  // per kernel launch boundary (ramp up / drain)
 // Fractions of the measured peaks the kernels sustain, measured on B200 with
 // CUDA events: the tcgen05 GEMM ran the fused MLP 8192x4096x16384 at
