@@ -166,6 +166,15 @@ def test_errors_are_loud(ops):
     assert rc == L.TFB200_EWORKSPACE and b"workspace" in L.lib().tfb200_last_error()
     with pytest.raises(TFB200Error):
         L.check(rc)
+    # Through the Python mirror: a workspace that is given but too small is refused (no hidden allocation),
+    # and so are operands on the host or spread over two devices, before anything is launched.
+    with pytest.raises(ValueError, match="workspace"):
+        ops.fused_rmsnorm_matmul(x, g, w, 1e-5, workspace=tiny[:16])
+    with pytest.raises(TypeError):
+        ops.fused_rmsnorm_matmul(x, g.cpu(), w, 1e-5)
+    if torch.cuda.device_count() > 1:
+        with pytest.raises(ValueError, match="cuda:1"):
+            ops.fused_rmsnorm_matmul(x, g, w.to("cuda:1"), 1e-5)
 
 
 # ------------------------------------------------------------ full-size workloads

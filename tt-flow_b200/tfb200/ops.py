@@ -71,9 +71,11 @@ def matmul(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None) ->
     b2 = _rows2d(b, "b")
     if a2.shape[1] != b2.shape[0]:
         raise ValueError(f"matmul: inner dimensions differ ({a2.shape[1]} vs {b2.shape[0]})")
+    dev = _device_of(("a", a), ("b", b), ("out", out))
     y = out if out is not None else torch.empty(a2.shape[0], b2.shape[1], dtype=torch.bfloat16, device=a.device)
-    L.check(L.lib().tfb200_matmul(ctypes.byref(mat(a2)), ctypes.byref(mat(b2)), ctypes.byref(mat(y)),
-                                  ctypes.c_void_p(stream_ptr())))
+    with torch.cuda.device(dev):
+        L.check(L.lib().tfb200_matmul(ctypes.byref(mat(a2)), ctypes.byref(mat(b2)), ctypes.byref(mat(y)),
+                                      ctypes.c_void_p(stream_ptr())))
     return y.reshape(*a.shape[:-1], b2.shape[1]) if out is None else y
 
 
@@ -82,9 +84,33 @@ def rmsnorm_matmul_workspace_bytes(m: int, k: int, n: int) -> int:
 
 
 def _workspace(need: int, ws: torch.Tensor | None, device) -> torch.Tensor:
-    if ws is not None and ws.numel() * ws.element_size() >= need:
-        return ws
-    return torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+    """The caller's workspace, checked, or (when none is given) a new one. A workspace that is given but too small
+    is an error, not a silent reallocation: callers pass one precisely to keep allocations out of their loop."""
+    if ws is None:
+        return torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+    if not ws.is_cuda or ws.device != device:
+        raise ValueError(f"workspace must be on {device} (got {ws.device})")
+    if not ws.is_contiguous():
+        raise ValueError("workspace must be contiguous")
+    if ws.numel() * ws.element_size() < need:
+        raise ValueError(f"workspace holds {ws.numel() * ws.element_size()} bytes; this call needs {need}")
+    return ws
+
+
+def _device_of(*named) -> torch.device:
+    """The one CUDA device of every operand given (name, tensor-or-None); the call then runs on that device's
+    current stream."""
+    dev = None
+    for name, t in named:
+        if t is None:
+            continue
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise TypeError(f"{name} must be a CUDA tensor")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"{name} is on {t.device}; the other operands are on {dev}")
+    return dev
 
 
 def fused_rmsnorm_matmul(x: torch.Tensor, gamma: torch.Tensor, w: torch.Tensor, eps: float = 1e-6,
@@ -96,12 +122,14 @@ def fused_rmsnorm_matmul(x: torch.Tensor, gamma: torch.Tensor, w: torch.Tensor, 
     if w2.shape[0] != K:
         raise ValueError(f"fused_rmsnorm_matmul: x has K={K} but w has {w2.shape[0]} rows")
     g = _vec(gamma, K, "gamma")
+    dev = _device_of(("x", x), ("gamma", gamma), ("w", w), ("out", out))
     y = out if out is not None else torch.empty(x2.shape[0], w2.shape[1], dtype=torch.bfloat16, device=x.device)
-    ws = _workspace(rmsnorm_matmul_workspace_bytes(x2.shape[0], K, w2.shape[1]), workspace, x.device)
-    L.check(L.lib().tfb200_fused_rmsnorm_matmul(ctypes.byref(mat(x2)), ctypes.c_void_p(g.data_ptr()),
-                                                ctypes.byref(mat(w2)), ctypes.c_float(eps), ctypes.byref(mat(y)),
-                                                ctypes.c_void_p(stream_ptr()), ctypes.c_void_p(ws.data_ptr()),
-                                                ctypes.c_size_t(ws.numel() * ws.element_size())))
+    ws = _workspace(rmsnorm_matmul_workspace_bytes(x2.shape[0], K, w2.shape[1]), workspace, dev)
+    with torch.cuda.device(dev):
+        L.check(L.lib().tfb200_fused_rmsnorm_matmul(ctypes.byref(mat(x2)), ctypes.c_void_p(g.data_ptr()),
+                                                    ctypes.byref(mat(w2)), ctypes.c_float(eps), ctypes.byref(mat(y)),
+                                                    ctypes.c_void_p(stream_ptr()), ctypes.c_void_p(ws.data_ptr()),
+                                                    ctypes.c_size_t(ws.numel() * ws.element_size())))
     return y.reshape(*x.shape[:-1], w2.shape[1]) if out is None else y
 
 
@@ -138,13 +166,16 @@ def fused_mlp(x: torch.Tensor, gamma: torch.Tensor, w1: torch.Tensor, b1: torch.
     g = _vec(gamma, K, "gamma")
     if gelu not in _GELU:
         raise ValueError(f"gelu must be 'erf' or 'tanh' (got {gelu!r})")
+    dev = _device_of(("x", x), ("gamma", gamma), ("w1", w1), ("b1", b1), ("w2", w2), ("residual", residual),
+                     ("out", out))
     y = out if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
-    workspace = _workspace(mlp_workspace_bytes(M, K, H, N), workspace, x.device)
-    L.check(L.lib().tfb200_fused_mlp(
-        ctypes.byref(mat(x2)), ctypes.c_void_p(g.data_ptr()), ctypes.byref(mat(W1)),
-        ctypes.c_void_p(b.data_ptr() if b is not None else None), ctypes.byref(mat(W2)), ctypes.byref(mat(r2)),
-        ctypes.c_float(eps), ctypes.c_int(_GELU[gelu]), ctypes.byref(mat(y)), ctypes.c_void_p(stream_ptr()),
-        ctypes.c_void_p(workspace.data_ptr()), ctypes.c_size_t(workspace.numel() * workspace.element_size())))
+    workspace = _workspace(mlp_workspace_bytes(M, K, H, N), workspace, dev)
+    with torch.cuda.device(dev):
+        L.check(L.lib().tfb200_fused_mlp(
+            ctypes.byref(mat(x2)), ctypes.c_void_p(g.data_ptr()), ctypes.byref(mat(W1)),
+            ctypes.c_void_p(b.data_ptr() if b is not None else None), ctypes.byref(mat(W2)), ctypes.byref(mat(r2)),
+            ctypes.c_float(eps), ctypes.c_int(_GELU[gelu]), ctypes.byref(mat(y)), ctypes.c_void_p(stream_ptr()),
+            ctypes.c_void_p(workspace.data_ptr()), ctypes.c_size_t(workspace.numel() * workspace.element_size())))
     return y.reshape(*x.shape[:-1], N) if out is None else y
 
 
@@ -162,13 +193,19 @@ def fused_mlp_partial(x: torch.Tensor, gamma: torch.Tensor, w1_shard: torch.Tens
         raise ValueError("fused_mlp_partial: shapes do not chain")
     b = _vec(b1_shard, H, "b1_shard")
     g = _vec(gamma, K, "gamma")
+    if gelu not in _GELU:
+        raise ValueError(f"gelu must be 'erf' or 'tanh' (got {gelu!r})")
+    dev = _device_of(("x", x), ("gamma", gamma), ("w1_shard", w1_shard), ("b1_shard", b1_shard),
+                     ("w2_shard", w2_shard), ("out", out))
     y = out if out is not None else torch.empty(M, N, dtype=torch.float32, device=x.device)
-    ws = _workspace(int(L.lib().tfb200_fused_mlp_partial_workspace_size(M, K, H, N)), workspace, x.device)
-    L.check(L.lib().tfb200_fused_mlp_partial(
-        ctypes.byref(mat(x2)), ctypes.c_void_p(g.data_ptr()), ctypes.byref(mat(W1)),
-        ctypes.c_void_p(b.data_ptr() if b is not None else None), ctypes.byref(mat(W2)), ctypes.c_float(eps),
-        ctypes.c_int(_GELU[gelu]), ctypes.c_void_p(y.data_ptr()), ctypes.c_int64(y.stride(0)),
-        ctypes.c_void_p(stream_ptr()), ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel())))
+    ws = _workspace(int(L.lib().tfb200_fused_mlp_partial_workspace_size(M, K, H, N)), workspace, dev)
+    with torch.cuda.device(dev):
+        L.check(L.lib().tfb200_fused_mlp_partial(
+            ctypes.byref(mat(x2)), ctypes.c_void_p(g.data_ptr()), ctypes.byref(mat(W1)),
+            ctypes.c_void_p(b.data_ptr() if b is not None else None), ctypes.byref(mat(W2)), ctypes.c_float(eps),
+            ctypes.c_int(_GELU[gelu]), ctypes.c_void_p(y.data_ptr()), ctypes.c_int64(y.stride(0)),
+            ctypes.c_void_p(stream_ptr()), ctypes.c_void_p(ws.data_ptr()),
+            ctypes.c_size_t(ws.numel() * ws.element_size())))
     return y
 
 
@@ -192,12 +229,15 @@ def fused_mlp_tp(x: torch.Tensor, gamma: torch.Tensor, w1_shard: torch.Tensor, b
         raise ValueError(f"gelu must be 'erf' or 'tanh' (got {gelu!r})")
     b = _vec(b1_shard, H, "b1_shard")
     g = _vec(gamma, K, "gamma")
-    ws = _workspace(int(L.lib().tfb200_fused_mlp_partial_workspace_size(M, K, H, N)), workspace, x.device)
-    L.check(L.lib().tfb200_fused_mlp_tp(
-        ctypes.byref(mat(x2)), ctypes.c_void_p(g.data_ptr()), ctypes.byref(mat(W1)),
-        ctypes.c_void_p(b.data_ptr() if b is not None else None), ctypes.byref(mat(W2)), ctypes.byref(mat(r2)),
-        ctypes.c_float(eps), ctypes.c_int(_GELU[gelu]), ctypes.byref(comm), ctypes.c_void_p(stream_ptr()),
-        ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel())))
+    dev = _device_of(("x", x), ("gamma", gamma), ("w1_shard", w1_shard), ("b1_shard", b1_shard),
+                     ("w2_shard", w2_shard), ("residual", residual))
+    ws = _workspace(int(L.lib().tfb200_fused_mlp_partial_workspace_size(M, K, H, N)), workspace, dev)
+    with torch.cuda.device(dev):
+        L.check(L.lib().tfb200_fused_mlp_tp(
+            ctypes.byref(mat(x2)), ctypes.c_void_p(g.data_ptr()), ctypes.byref(mat(W1)),
+            ctypes.c_void_p(b.data_ptr() if b is not None else None), ctypes.byref(mat(W2)), ctypes.byref(mat(r2)),
+            ctypes.c_float(eps), ctypes.c_int(_GELU[gelu]), ctypes.byref(comm), ctypes.c_void_p(stream_ptr()),
+            ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel() * ws.element_size())))
 
 
 def residual_add(partial: torch.Tensor, residual: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -207,7 +247,10 @@ def residual_add(partial: torch.Tensor, residual: torch.Tensor, out: torch.Tenso
     r2 = _rows2d(residual, "residual")
     if tuple(r2.shape) != tuple(partial.shape):
         raise ValueError("residual and partial shapes differ")
+    dev = _device_of(("partial", partial), ("residual", residual), ("out", out))
     y = out if out is not None else torch.empty(r2.shape, dtype=torch.bfloat16, device=partial.device)
-    L.check(L.lib().tfb200_residual_add(ctypes.c_void_p(partial.data_ptr()), ctypes.c_int64(partial.stride(0)),
-                                        ctypes.byref(mat(r2)), ctypes.byref(mat(y)), ctypes.c_void_p(stream_ptr())))
+    with torch.cuda.device(dev):
+        L.check(L.lib().tfb200_residual_add(ctypes.c_void_p(partial.data_ptr()), ctypes.c_int64(partial.stride(0)),
+                                            ctypes.byref(mat(r2)), ctypes.byref(mat(y)),
+                                            ctypes.c_void_p(stream_ptr())))
     return y

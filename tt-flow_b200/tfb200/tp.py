@@ -67,9 +67,11 @@ class TPDecodeMLP:
                  group=None):
         import torch
 
+        from . import _lib as L
         from . import ops
 
         self.ops = ops
+        self.L = L
         self.shard = shard_mlp(w1, b1, w2, rank, world)
         self.gamma = gamma
         self.eps = eps
@@ -84,6 +86,10 @@ class TPDecodeMLP:
         M, N = x.shape[0], shard.w2.shape[1]
         if self._part is None or tuple(self._part.shape) != (M, N):
             self._part = self.torch.empty(M, N, dtype=self.torch.float32, device=x.device)
+        K, H = shard.w1.shape
+        need = int(self.L.lib().tfb200_fused_mlp_partial_workspace_size(M, K, H, N))
+        if self._ws is None or self._ws.numel() < need:  # allocated once per shape growth, not per call
+            self._ws = self.torch.empty(max(need, 256), dtype=self.torch.uint8, device=x.device)
         return self.ops.fused_mlp_partial(x, self.gamma, shard.w1, shard.b1, shard.w2, self.eps, self.gelu,
                                           out=self._part, workspace=self._ws)
 
