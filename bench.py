@@ -278,7 +278,8 @@ def run_reference(args) -> int:
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": float(np.median(secs)) * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong" if unit == "GB/s" else "weak", "vs_baseline": None,
+        "dtype": "f32",
         "data": "synthetic (seeded numpy, bf16-rounded inputs)",
         "config": {"workload": name, **d, "gelu": "erf (the reference golden's only form)", "eps": 1e-5,
                    "sample_rows_per_step": info["rows"]},

@@ -1,0 +1,42 @@
+"""The reference arm of bench.py (the reference's CPU golden, restated) keeps the
+bench contract: one JSON line with the metric, its unit, the timing fields, the
+CPU-baseline description and an e2e block without host transfers; under
+torchrun only rank 0 prints. Runs on the host cores, on the small MLP workload."""
+
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _run(extra_env=None, *args):
+    env = dict(os.environ)
+    env.update(extra_env or {})
+    return subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", *args],
+                          capture_output=True, text=True, env=env, timeout=300, cwd=ROOT)
+
+
+def test_reference_arm_prints_one_contract_line():
+    r = _run(None, "--workload", "mlp_block_small", "--steps", "2", "--warmup", "1", "--ref-rows", "64")
+    assert r.returncode == 0, r.stderr
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["unit"] == "TFLOP/s" and d["value"] > 0
+    for key in ("metric", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling", "vs_baseline",
+                "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["steps"] == 2 and d["warmup"] == 1 and d["higher_is_better"] is True
+    assert d["config"]["workload"] == "mlp_block_small"
+    cb = d["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    r = _run({"RANK": "1", "WORLD_SIZE": "2"}, "--workload", "mlp_block_small", "--steps", "1", "--warmup", "0")
+    assert r.returncode == 0, r.stderr
+    assert not [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
