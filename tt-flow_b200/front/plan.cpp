@@ -33,6 +33,7 @@ constexpr double kLaunchSeconds = 3e-6;  // per kernel launch boundary (ramp up 
 // 1428-1466 TFLOP/s (87-90 % of 1635.3) and the fused RMSNorm+MatMul
 // 8192x4096x6144 at 1398 TFLOP/s (85.5 %); the weight-streaming kernels ran the
 // decode MLP 32x8192x28672 at 5262-5331 GB/s (80.5-81.6 % of 6534.5).
+// (spec/devices.json "model" records both with their basis.)
 constexpr double kTensorEfficiency = 0.87;
 constexpr double kHbmEfficiency = 0.81;
 
@@ -195,7 +196,7 @@ B200Plan plan_b200(const PlanRequest& r) {
                               "% full: a stream-K split of the tail would balance the SMs");
     if (M % kTileM != 0) p.suggestions.push_back("M is not a multiple of 128: the last row tile is partly empty");
   }
-  if (p.bottleneck == "compute" && !stream)
+  if (p.bottleneck == "compute" && p.mapping == "persistent-cta-tiles")
     p.suggestions.push_back("tensor-bound: 2-CTA (cta_group::2) tiles halve B-operand shared-memory traffic");
   return p;
 }

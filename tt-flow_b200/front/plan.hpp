@@ -13,6 +13,8 @@
 
 namespace tfb200::front {
 
+// The B200 entry of spec/devices.json (the reference's device-table layout);
+// tests/test_device_spec.py holds these values and the time model to it.
 struct B200Device {
   std::string name = "b200";
   std::string arch = "blackwell_sm100a";
