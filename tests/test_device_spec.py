@@ -80,3 +80,19 @@ def test_plan_device_block_and_time_model_follow_the_entry(lit):
     est = max(flops / (meas["bf16_flops_per_second"] * model["tensor_efficiency"]),
               hbm / (meas["hbm_bytes_per_second"] * model["hbm_efficiency"])) + launches * model["launch_seconds"]
     assert abs(plan["perf"]["est_cycles"] - est * B200["clock_hz"]) <= 1
+
+
+def test_python_lookup_reads_the_same_entry():
+    import sys
+
+    sys.path.insert(0, str(ROOT / "tt-flow_b200"))
+    from tfb200 import devices
+
+    d = devices.lookup("b200")
+    assert devices.DEFAULT_DEVICE == "b200" and devices.lookup("hgx-b200") is d
+    assert d.total_cores == 148 and d.cb_budget() == B200["l1"]["usable_bytes"]
+    assert d.flops_per_cycle_per_core == B200["matrix_unit"]["flops_per_cycle_per_core"]
+    assert d.measured_bf16_flops_per_second == B200["measured"]["bf16_flops_per_second"]
+    assert devices.all_devices() == (d,)
+    with pytest.raises(KeyError, match="valid devices: b200"):
+        devices.lookup("n150")
