@@ -88,14 +88,20 @@ constexpr size_t smem_bytes() {
   return 1024 /*alignment slack*/ + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + sizeof(SmemCtl);
 }
 
-__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm, int& tn) {
-  const int per_group = GROUP_M * num_n;
+// Grouped raster: tiles run down `group` row tiles before moving one column
+// tile right, so concurrently running tiles share A and B panels in L2.
+template <int GROUP>
+__device__ __forceinline__ void tile_coords_g(int t, int num_m, int num_n, int& tm, int& tn) {
+  const int per_group = GROUP * num_n;
   const int g = t / per_group;
-  const int first_m = g * GROUP_M;
-  const int gsize = min(num_m - first_m, GROUP_M);
+  const int first_m = g * GROUP;
+  const int gsize = min(num_m - first_m, GROUP);
   const int local = t - g * per_group;
   tm = first_m + local % gsize;
   tn = local / gsize;
+}
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm, int& tn) {
+  tile_coords_g<GROUP_M>(t, num_m, num_n, tm, tn);
 }
 
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
@@ -503,6 +509,8 @@ __device__ __forceinline__ void raise_abort_pair(PairCtl* ctl, int* status) {
   atomicExch(status, kDevTimeout);
 }
 
+// GROUP: raster group (row tiles) of the pair tiles; see launch_pair.
+template <int GROUP>
 __global__ void __launch_bounds__(256, 1)
     k_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const KParams p) {
@@ -564,7 +572,7 @@ __global__ void __launch_bounds__(256, 1)
       bool ok = true;
       for (int t = pair; t < total && ok; t += npairs) {
         int tm, tn;
-        tile_coords(t, num_m, num_n, tm, tn);
+        tile_coords_g<GROUP>(t, num_m, num_n, tm, tn);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(smem_u32(&ctl->empty[stage]), phase ^ 1u, &ctl->abort, p.timeout_ns)) {
             raise_abort_pair(ctl, p.status);
@@ -648,7 +656,7 @@ __global__ void __launch_bounds__(256, 1)
     int i = 0;
     for (int t = pair; t < total; t += npairs, ++i) {
       int tm, tn;
-      tile_coords(t, num_m, num_n, tm, tn);
+      tile_coords_g<GROUP>(t, num_m, num_n, tm, tn);
       const int acc = i & 1;
       const uint32_t use = static_cast<uint32_t>(i >> 1);
       bool ok = mbar_wait(smem_u32(&ctl->tfull[acc]), use & 1u, &ctl->abort, p.timeout_ns);
@@ -798,8 +806,10 @@ int launch(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int 
   return 0;
 }
 
-int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
-                int pair_tiles, cudaStream_t s, std::string* err) {
+template <int GROUP>
+int launch_pair_g(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                  int pair_tiles, cudaStream_t s, std::string* err) {
+  const auto kern = k_gemm_pair<GROUP>;
   // Per-device first-call setup; calls may come from several host threads.
   static std::mutex mu;
   static std::atomic<bool> ready[64];
@@ -815,8 +825,8 @@ int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb,
   if (!ready[dev].load(std::memory_order_acquire)) lock.lock();
   if (!ready[dev].load(std::memory_order_relaxed)) {
     cudaError_t e =
-        cudaFuncSetAttribute(k_gemm_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemm_pair, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
     if (e != cudaSuccess) {
       if (err) *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
       return -3;
@@ -834,7 +844,7 @@ int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb,
     q.attrs = qa;
     q.numAttrs = 1;
     int n = 0;
-    e = cudaOccupancyMaxActiveClusters(&n, k_gemm_pair, &q);
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &q);
     if (e != cudaSuccess || n <= 0) {
       if (err) *err = std::string("cudaOccupancyMaxActiveClusters: ") + cudaGetErrorString(e);
       return -3;
@@ -858,7 +868,7 @@ int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb,
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_pair, ta, tb, tc, kp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, kp);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     if (err) *err = std::string("pair gemm launch: ") + cudaGetErrorString(e);
@@ -866,6 +876,16 @@ int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb,
   }
   count_launch();
   return 0;
+}
+
+// Long-K products (K >= 8192, such as the MLP down-projection) run with raster
+// groups of 8 row tiles, the rest with 16. In a burst A/B on one GPU, groups of
+// 8 ran the 8192x16384x4096 down-projection 1.1 % faster; the 8192x4096x16384
+// up-projection keeps 16.
+int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                int pair_tiles, cudaStream_t s, std::string* err) {
+  return kp.K >= 8192 ? launch_pair_g<8>(kp, ta, tb, tc, pair_tiles, s, err)
+                      : launch_pair_g<GROUP_M>(kp, ta, tb, tc, pair_tiles, s, err);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
