@@ -42,7 +42,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # ncu captures summarised in profiles/k_gemm_mlp_8192x4096x16384.md and
 # profiles/k_stream_decode_mlp_32x8192x28672.md.
 TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {
-    "mlp_8192x4096x16384": (437.492e6 + 251.886e6 + 1466.364e6 + 61.881e6) / 2,
+    "mlp_8192x4096x16384": (439.884e6 + 253.001e6 + 1326.001e6 + 62.057e6) / 2,
     "decode_mlp_32x8192x28672": (476.727e6 + 8.738e6 + 474.788e6 + 4.495e6) / 2,
 }
 
