@@ -17,7 +17,8 @@ ROOT = Path(__file__).resolve().parents[1]
 TOOL = ROOT / "tt-flow_b200" / "bin" / "tfb200-opt"
 SUPPORTED = {"--tensixflow-device=b200", "--tensixflow-fuse-rmsnorm-matmul", "--tensixflow-plan-noc-sharding",
              "--tensixflow-allocate-circular-buffers", "--tensixflow-to-json", "-verify-diagnostics",
-             "--tensixflow-import-ttir", "--allow-unregistered-dialect"}
+             "--tensixflow-import-ttir", "--allow-unregistered-dialect", "--canonicalize",
+             "--tensixflow-canonicalize"}
 
 
 def filecheck() -> str | None:

@@ -31,7 +31,7 @@ REF_TESTS = Path("/root/reference/test/Tensixflow")
 # emission.
 REF_FILES = ["attrs.mlir", "dialect_parse.mlir", "smoke.mlir", "ops.mlir", "matmul.mlir", "rmsnorm.mlir",
              "shape_inference.mlir", "fused_ops.mlir", "fuse_rmsnorm_matmul.mlir", "fuse_mlp.mlir",
-             "fusion_tracking.mlir", "import_ttir.mlir", "import_ttir_negative.mlir"]
+             "fusion_tracking.mlir", "import_ttir.mlir", "import_ttir_negative.mlir", "canonicalize.mlir"]
 
 
 @pytest.fixture(scope="module", autouse=True)

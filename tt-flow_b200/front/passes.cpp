@@ -9,6 +9,9 @@
 //       tensixflow.schedule and tensixflow.emission (PlanNocShardingPass.cpp:135-304)
 //   --tensixflow-allocate-circular-buffers   fills the schedule's buffer list
 //       (shared-memory rings and TMEM accumulators; AllocateCircularBuffersPass.cpp:63-104)
+//   --canonicalize, --tensixflow-canonicalize   identity-add removal: add %x, zero-splat
+//       constant (either operand) -> %x, then dead constants dropped
+//       (TensixflowOps.cpp hasCanonicalizer pattern, test/Tensixflow/canonicalize.mlir)
 //   --tensixflow-to-json               plan JSON instead of IR (tensixflow-translate.cpp:75-222)
 //   --tensixflow-device=<name>         device selection (DeviceSelection.cpp:26-49); b200 only
 //   --tensixflow-import-ttir           bare-tensor TTIR in (ttir_import.cpp)
@@ -112,6 +115,39 @@ bool try_fuse_rms_mm(Module& m, Func& f, Op* rms) {
   erase_op(mm);
   erase_op(rms);
   return true;
+}
+
+// A splat constant whose value is +0 or -0 ("dense<0.000000e+00> : tensor<...>").
+bool zero_splat(const Op* op) {
+  if (!op || op->name != "tensixflow.constant") return false;
+  const auto it = op->attrs.find("value");
+  if (it == op->attrs.end() || it->second.rfind("dense<", 0) != 0) return false;
+  const size_t close = it->second.find('>');
+  const std::string lit = it->second.substr(6, close == std::string::npos ? std::string::npos : close - 6);
+  if (lit.empty() || lit[0] == '[' || lit[0] == '"') return false;  // not a scalar splat
+  char* end = nullptr;
+  const double v = std::strtod(lit.c_str(), &end);
+  return end && *end == '\0' && v == 0.0;
+}
+
+// add %x, %zero and add %zero, %x become %x; constants left without users go.
+void canonicalize_pass(Module& m) {
+  for (Func& f : m.funcs) {
+    for (Op* op : f.body) {
+      if (op->erased || op->name != "tensixflow.add" || op->operands.size() != 2) continue;
+      for (int z = 0; z < 2; ++z) {
+        Value* zero = op->operands[z];
+        Value* keep = op->operands[1 - z];
+        if (zero_splat(zero->def) && keep->type == op->result->type) {
+          replace_all_uses(op->result, keep);
+          erase_op(op);
+          break;
+        }
+      }
+    }
+    for (Op* op : f.body)
+      if (!op->erased && op->name == "tensixflow.constant" && op->result->users.empty()) erase_op(op);
+  }
 }
 
 void fuse_pass(Module& m) {
@@ -326,7 +362,8 @@ PipelineResult run_pipeline(const std::string& text, const std::vector<std::stri
     } else if (a == "--tensixflow-to-json") {
       to_json = true;
     } else if (a == "--tensixflow-fuse-rmsnorm-matmul" || a == "--tensixflow-plan-noc-sharding" ||
-               a == "--tensixflow-allocate-circular-buffers") {
+               a == "--tensixflow-allocate-circular-buffers" || a == "--canonicalize" ||
+               a == "--tensixflow-canonicalize") {
       passes.push_back(a);
     } else {
       res.diag = "unknown option '" + a + "'";
@@ -351,7 +388,9 @@ PipelineResult run_pipeline(const std::string& text, const std::vector<std::stri
   B200Plan plan;
   bool planned = false;
   for (const std::string& p : passes) {
-    if (p == "--tensixflow-fuse-rmsnorm-matmul") {
+    if (p == "--canonicalize" || p == "--tensixflow-canonicalize") {
+      canonicalize_pass(*m);
+    } else if (p == "--tensixflow-fuse-rmsnorm-matmul") {
       fuse_pass(*m);
     } else if (p == "--tensixflow-plan-noc-sharding") {
       PlanRequest req;
