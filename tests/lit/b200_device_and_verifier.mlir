@@ -6,7 +6,7 @@
 
 //--- ok.mlir
 // The B200 backend plans for b200 only; a Tensix device name is refused.
-// DEV: unknown or unsupported device 'n150' for the B200 backend (supported: b200)
+// DEV: unknown device 'n150'; valid devices: b200
 tensixflow.func @mm(%a: tensor<128x64xbf16>, %b: tensor<64x32xbf16>) -> tensor<128x32xbf16> {
   %0 = tensixflow.matmul %a, %b : tensor<128x64xbf16> x tensor<64x32xbf16> -> tensor<128x32xbf16>
   tensixflow.return %0 : tensor<128x32xbf16>

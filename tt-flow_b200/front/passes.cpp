@@ -371,7 +371,7 @@ PipelineResult run_pipeline(const std::string& text, const std::vector<std::stri
     }
   }
   if (device != "b200") {
-    res.diag = "unknown or unsupported device '" + device + "' for the B200 backend (supported: b200)";
+    res.diag = "unknown device '" + device + "'; valid devices: b200";  // the reference's wording (Scheduler/DeviceSelection.cpp:35)
     return res;
   }
   std::string err;
