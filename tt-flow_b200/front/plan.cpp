@@ -191,7 +191,10 @@ B200Plan plan_b200(const PlanRequest& r) {
       p.suggestions.push_back("fewer output tiles (" + std::to_string(p.tiles) +
                               ") than SMs: use smaller tiles or split K to fill the 148 SMs");
     const double waves = static_cast<double>(p.tiles) / static_cast<double>(d.sms());
-    if (waves > 1.0 && waves - std::floor(waves) > 0 && waves - std::floor(waves) < 0.5)
+    // (Not for the CTA-pair kernel: splitting its last wave into half tiles measured slower on the B200, whose
+    // idle SMs in a short last wave let the busy ones clock higher under the power limit.)
+    if (p.mapping != "persistent-cta-pair-tiles" && waves > 1.0 && waves - std::floor(waves) > 0 &&
+        waves - std::floor(waves) < 0.5)
       p.suggestions.push_back("last wave runs " + std::to_string(static_cast<int>((waves - std::floor(waves)) * 100)) +
                               "% full: a stream-K split of the tail would balance the SMs");
     if (M % kTileM != 0) p.suggestions.push_back("M is not a multiple of 128: the last row tile is partly empty");
