@@ -224,6 +224,22 @@ def test_time_model_tracks_measurement(lit):
     assert abs(est_s / MEASURED_S[lit] - 1.0) < 0.15, (est_s, MEASURED_S[lit])
 
 
+# Kernel time per step from the ncu launch lists summarised in profiles/ (every kernel of the step, serialised,
+# cold L2): fused MLP 8192x4096x16384 = k_gemm_pair 14177.7 us / 10 steps + k_rms_prep_reg 201.7 us / 10 steps;
+# decode MLP 32x8192x28672 = k_stream 1810.7 us / 10 steps + k_rms_prep_rows 44.7 us / 10 steps.
+NCU_S = {"b200_plan_mlp.mlir": (14177.7 + 201.7) / 10 * 1e-6, "b200_plan_decode.mlir": (1810.7 + 44.7) / 10 * 1e-6}
+
+
+@pytest.mark.parametrize("lit", sorted(NCU_S))
+def test_time_model_tracks_ncu(lit):
+    """The roofline model against the ncu-measured kernel time of the same step."""
+    text = (ROOT / "tests" / "lit" / lit).read_text()
+    rc, out, err = _opt(text, "--tensixflow-fuse-rmsnorm-matmul", "--tensixflow-to-json")
+    assert rc == 0, err
+    est_s = json.loads(out)["perf"]["est_cycles"] / 1.965e9
+    assert abs(est_s / NCU_S[lit] - 1.0) < 0.15, (est_s, NCU_S[lit])
+
+
 def test_lit_runner_not_inverts_only_the_tool(tmp_path):
     """`not tool | FileCheck` must still fail when FileCheck fails: a wrong CHECK is reported."""
     bad = tmp_path / "bad.mlir"
