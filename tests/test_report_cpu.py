@@ -132,3 +132,18 @@ def test_a_reference_plan_replanned_for_b200_passes_the_report(tmp_path):
     r, html = _report(tmp_path, json.loads(buf.value.decode()), "replanned")
     assert r.returncode == 0, r.stderr
     assert "persistent-cta-pair-tiles" in html.read_text()
+
+
+def test_translate_name_reads_planned_ir_from_stdin():
+    """tensixflow-translate --tensixflow-to-json reads the planned module on stdin; tfb200-translate (the same
+    tool under that name, for TENSIXFLOW_TRANSLATE_BIN) gives the plan JSON tfb200-opt gives."""
+    if not (BIN / "tfb200-translate").exists():
+        subprocess.run(["make", "-C", str(ROOT / "tt-flow_b200"), "bin/tfb200-translate"], check=True,
+                       capture_output=True)
+    lit = LIT / "b200_plan_mlp.mlir"
+    planned = subprocess.run([str(BIN / "tfb200-opt"), "--tensixflow-device=b200", "--tensixflow-fuse-rmsnorm-matmul",
+                              "--tensixflow-plan-noc-sharding", "--tensixflow-allocate-circular-buffers", str(lit)],
+                             capture_output=True, text=True, check=True).stdout
+    via_translate = subprocess.run([str(BIN / "tfb200-translate"), "--tensixflow-to-json"], input=planned,
+                                   capture_output=True, text=True, check=True).stdout
+    assert json.loads(via_translate) == _plan("b200_plan_mlp.mlir")
