@@ -5,8 +5,11 @@
 One step = one pass of the hot path over one batch: for the default workload,
 the fused MLP block y = X + GELU(RMSNorm(X) @ W1 + b1) @ W2 at 8192 tokens x
 d=4096 x hidden=16384, bf16 I/O, fp32 accumulation, tanh GELU, eps 1e-5. Under
-torchrun each rank owns 8192 rows of a (8192 * N)-row batch with the weights
-replicated and no collective (weak scaling). Timing: W untimed warm-up steps,
+torchrun the 8192 token rows are split into N contiguous blocks, one per rank,
+with the weights replicated and no collective (strong scaling: the job's work
+is fixed, `value` is the whole job's TFLOP/s); `--scaling weak` gives every
+rank its own 8192 rows instead. `--shard-of N` times, on one GPU, the share
+one rank has in an N-way split. Timing: W untimed warm-up steps,
 then exactly K steps between barrier + synchronize pairs, CUDA events on the
 launching stream, max over ranks. Inputs (W1 + W2 + X = 320 MiB) exceed the
 126 MB L2, so no flush is needed between steps.
@@ -278,7 +281,8 @@ def run_reference(args) -> int:
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": float(np.median(secs)) * 1e3,
-        "higher_is_better": True, "scaling": "strong" if unit == "GB/s" else "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if (unit == "GB/s" or args.scaling == "strong") else "weak",
+        "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded numpy, bf16-rounded inputs)",
         "config": {"workload": name, **d, "gelu": "erf (the reference golden's only form)", "eps": 1e-5,
@@ -368,7 +372,18 @@ def run_ours(args) -> int:
     name = args.workload
     wl = W.WORKLOADS[name]
     d = wl.dims
-    t = W.generate(name)
+    tp_shape = wl.kind == "fused_mlp" and d["M"] <= 64
+    # Row sharding of the prefill workloads: rank r of `parts` owns rows [lo, hi) of the workload's rows.
+    parts = world if args.shard_of <= 0 else args.shard_of
+    strong = not tp_shape and args.scaling == "strong" and parts > 1
+    if strong:
+        r = rank if args.shard_of <= 0 else 0
+        lo, hi = d["M"] * r // parts, d["M"] * (r + 1) // parts
+        t = W.generate(name, rows=(lo, hi))
+    else:
+        lo, hi = 0, d["M"]
+        t = W.generate(name)
+    rows_here = hi - lo
 
     def dev(a):
         return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda().view(torch.bfloat16)
@@ -398,8 +413,9 @@ def run_ours(args) -> int:
     elif wl.kind == "fused_mlp":
         # One GPU (the decode shape included: the C ABI picks the weight-streaming kernels for few rows).
         x, g, w1, b1, w2 = (dev(t[k]) for k in ("x", "gamma", "w1", "b1", "w2"))
-        y = torch.empty(d["M"], d["N"], dtype=torch.bfloat16, device="cuda")
-        ws = torch.empty(ops.mlp_workspace_bytes(d["M"], d["K"], d["H"], d["N"]), dtype=torch.uint8, device="cuda")
+        y = torch.empty(rows_here, d["N"], dtype=torch.bfloat16, device="cuda")
+        ws = torch.empty(ops.mlp_workspace_bytes(rows_here, d["K"], d["H"], d["N"]), dtype=torch.uint8,
+                         device="cuda")
 
         def step(xin=None, yout=None):
             xx = x if xin is None else xin
@@ -408,8 +424,9 @@ def run_ours(args) -> int:
         in_bytes = x.numel() * 2
     elif wl.kind == "fused_rmsnorm_matmul":
         x, g, w = (dev(t[k]) for k in ("x", "gamma", "w"))
-        y = torch.empty(d["M"], d["N"], dtype=torch.bfloat16, device="cuda")
-        ws = torch.empty(ops.rmsnorm_matmul_workspace_bytes(d["M"], d["K"], d["N"]), dtype=torch.uint8, device="cuda")
+        y = torch.empty(rows_here, d["N"], dtype=torch.bfloat16, device="cuda")
+        ws = torch.empty(ops.rmsnorm_matmul_workspace_bytes(rows_here, d["K"], d["N"]), dtype=torch.uint8,
+                         device="cuda")
 
         def step(xin=None, yout=None):
             return ops.fused_rmsnorm_matmul(x if xin is None else xin, g, w, wl.eps, out=y if yout is None else yout,
@@ -417,12 +434,13 @@ def run_ours(args) -> int:
         in_bytes = x.numel() * 2
     else:
         x, b = dev(t["a"]), dev(t["b"])
-        y = torch.empty(d["M"], d["N"], dtype=torch.bfloat16, device="cuda")
+        y = torch.empty(x.shape[0], d["N"], dtype=torch.bfloat16, device="cuda")
 
         def step(xin=None, yout=None):
             return ops.matmul(x if xin is None else xin, b, out=y if yout is None else yout)
         in_bytes = x.numel() * 2
-    flops_step = W.flops(name)
+    flops_step = W.flops(name)  # the whole workload (all ranks together)
+    flops_here = flops_step * rows_here // d["M"] if not tp_shape else flops_step
 
     def barrier():
         if world > 1:
@@ -456,6 +474,10 @@ def run_ours(args) -> int:
         # strong scaling: all ranks together stream the workload's bytes once per step
         bytes_step = W.algorithmic_bytes(name)
         value = bytes_step / (ms_step * 1e-3) / 1e9
+    elif args.shard_of > 0:
+        value = flops_here / (ms_step * 1e-3) / 1e12  # one rank's share, timed alone
+    elif strong:
+        value = flops_step / (ms_step * 1e-3) / 1e12  # the whole job's rows over the slowest rank's time
     else:
         value = flops_step * world / (ms_step * 1e-3) / 1e12
 
@@ -470,6 +492,8 @@ def run_ours(args) -> int:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ems = float(tt.item())
     e2e_value = (W.algorithmic_bytes(name) / (ems / args.steps * 1e-3) / 1e9 if tp
+                 else flops_here / (ems / args.steps * 1e-3) / 1e12 if args.shard_of > 0
+                 else flops_step / (ems / args.steps * 1e-3) / 1e12 if strong
                  else flops_step * world / (ems / args.steps * 1e-3) / 1e12)
 
     pk, pk_src = peaks()
@@ -495,25 +519,37 @@ def run_ours(args) -> int:
     else:
         unit = "TFLOP/s"
         peak = pk["bf16_tflops_sustained"] if sustained else pk["bf16_tflops"]
-        per_gpu = flops_step / (ms_step * 1e-3) / 1e12
+        per_gpu = flops_here / (ms_step * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s", "frac": per_gpu / peak,
-                "traffic": TRAFFIC_BYTES_PER_LAUNCH.get(name), "kernel": "k_gemm_pair (persistent cta_group::2 tcgen05 GEMM)",
+                "traffic": TRAFFIC_BYTES_PER_LAUNCH.get(name) if rows_here == d["M"] else None,
+                "kernel": "k_gemm_pair (persistent cta_group::2 tcgen05 GEMM)",
                 "launches_per_step": launches_per_step,
                 "peak_source": f"{pk_src} {'sustained' if sustained else 'burst'} bf16 (MEASURED_PEAKS.json)"
                 if pk_src == "measured" else "fallback"}
-        scaling = "weak"
-        parallelism = f"rows sharded over {world} GPU(s), weights replicated, no collective"
+        if args.shard_of > 0:
+            scaling = "strong"
+            parallelism = (f"one GPU timing rank 0's share ({rows_here} of {d['M']} rows) of a {parts}-way row split, "
+                           f"weights replicated")
+        elif strong:
+            scaling = "strong"
+            parallelism = (f"{d['M']} rows split over {world} GPUs ({rows_here} per GPU), weights replicated, "
+                           f"no collective")
+        else:
+            scaling = "weak"
+            parallelism = f"{d['M']} rows per GPU on {world} GPU(s), weights replicated, no collective"
     line = {
         "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": scaling,
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded numpy normal/uniform, bf16)",
         "config": {"workload": name, **d, "gelu": wl.gelu, "eps": wl.eps,
-                   "rows_per_gpu": d["M"] if not tp else d["M"],
-                   "global_rows": d["M"] * world if not tp else d["M"],
-                   "parallelism": parallelism, "l2": "inputs larger than L2 (no flush)"},
+                   "rows_per_gpu": rows_here,
+                   "global_rows": d["M"] * world if (not tp and not strong and args.shard_of <= 0) else d["M"],
+                   "parallelism": parallelism,
+                   "l2": "weights and activations larger than L2 (no flush)" if rows_here * d["K"] * 2 > 126e6
+                   else "weights larger than L2 (no flush); activations of the share fit"},
         "roofline": roof,
-        "e2e": {"value": e2e_value, "unit": unit, "h2d_bytes_per_step": in_bytes,
-                "d2h_bytes_per_step": y.numel() * 2,
+        "e2e": {"value": e2e_value, "unit": unit, "h2d_bytes_per_step": in_bytes * (world if strong else 1),
+                "d2h_bytes_per_step": y.numel() * 2 * (world if strong else 1),
                 "note": "public call with host buffers: X copied in from pinned host memory and Y copied back every "
                         "step, on copy streams overlapping the neighbouring steps' compute (double-buffered); "
                         "weights resident"},
@@ -554,6 +590,11 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp-reduce", choices=["fused", "nccl"], default="fused",
                     help="decode workloads: cross-GPU reduction inside the kernel, or an NCCL all-reduce")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="prefill workloads under torchrun: split the workload's rows over the ranks (strong) or "
+                         "give every rank all of them (weak)")
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="time rank 0's share of an N-way row split on this one GPU (prefill workloads)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

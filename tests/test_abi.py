@@ -45,15 +45,27 @@ def test_library_exports_every_declared_symbol(L):
 def test_version_and_workspace(L):
     lib = L.lib()
     assert lib.tfb200_version() == 1
+    # Above 128 rows the CTA-pair GEMM may split the tail of its last wave over idle pairs: the workspace adds
+    # the split's flags (128 slots x 64 int32, per GEMM) and up to 128 fp32 slots of 2 x 128 x 256 (or 4 per tile).
+    flags, slot = 128 * 64 * 4, 2 * 128 * 256 * 4
     # hidden block + staged bf16(x * gamma) + per-row inverse RMS, each 256-byte aligned
-    assert lib.tfb200_fused_mlp_workspace_size(8192, 4096, 16384, 4096) == 8192 * 16384 * 2 + 8192 * 4096 * 2 + 8192 * 4
+    base = 8192 * 16384 * 2 + 8192 * 4096 * 2 + 8192 * 4
+    assert lib.tfb200_fused_mlp_workspace_size(8192, 4096, 16384, 4096) == base + 2 * flags + 128 * slot
     assert lib.tfb200_fused_mlp_workspace_size(0, 4096, 16384, 4096) == 0
     # few rows: the streamed path adds fp32 accumulators and column-block counters
     assert lib.tfb200_fused_mlp_workspace_size(3, 8, 5, 8) == 7 * 256
     assert lib.tfb200_fused_mlp_partial_workspace_size(3, 8, 5, 8) == 6 * 256
-    assert lib.tfb200_fused_rmsnorm_matmul_workspace_size(8192, 4096, 6144) == 8192 * 4096 * 2 + 8192 * 4
+    # 128 rows run on the one-CTA kernel: no split region
+    assert lib.tfb200_fused_mlp_workspace_size(128, 128, 128, 128) == 128 * 128 * 2 + 128 * 128 * 2 + 512
+    assert lib.tfb200_fused_rmsnorm_matmul_workspace_size(8192, 4096, 6144) == (8192 * 4096 * 2 + 8192 * 4 + flags
+                                                                               + 128 * slot)
+    # one 256 x 256 tile: at most 4 parts
+    assert lib.tfb200_fused_rmsnorm_matmul_workspace_size(200, 64, 256) == 200 * 64 * 2 + 1024 + flags + 4 * slot
     # the staged block's leading dimension is rounded up to 8 elements for TMA
     assert lib.tfb200_fused_rmsnorm_matmul_workspace_size(100, 50, 7) == 11264 + 512  # 100*56*2 -> 11264
+    # absurd sizes saturate instead of wrapping around
+    assert lib.tfb200_fused_mlp_workspace_size(1 << 40, 4096, 16384, 4096) == 2 ** 64 - 1
+    assert lib.tfb200_fused_rmsnorm_matmul_workspace_size(4096, 1 << 40, 64) == 2 ** 64 - 1
 
 
 def test_host_validation_needs_no_device(L):

@@ -30,6 +30,7 @@ def test_reference_arm_prints_one_contract_line():
                 "dtype", "data", "config", "cpu_baseline", "e2e"):
         assert key in d, key
     assert d["steps"] == 2 and d["warmup"] == 1 and d["higher_is_better"] is True
+    assert d["scaling"] == "strong"  # the same config as the GPU arm: the workload's rows split over the GPUs
     assert d["config"]["workload"] == "mlp_block_small"
     cb = d["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]

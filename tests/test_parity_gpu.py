@@ -1,9 +1,9 @@
 """Parity of the sm_100a kernels (through the C ABI) against the oracle.
 
 Small workloads are compared over the whole output with the reference's own
-golden output (fixtures); the full-size workloads are compared row by row on a
-sample of rows (each output row depends only on its input row), against the
-fixtures' rows and against the oracle on further rows. Bar: max |y - golden| /
+golden output (fixtures); the full-size workloads are compared on every row
+with the oracle (tanh GELU, the benchmark's form) and on the fixtures' rows with
+the reference's own golden output (erf GELU). Bar: max |y - golden| /
 rms(golden) <= 2e-2 and PCC >= 0.9999 (tfb200.metrics), with non-vacuity checks:
 the output is bf16 and differs from the fp32 golden.
 """
@@ -180,26 +180,76 @@ def test_errors_are_loud(ops):
 # ------------------------------------------------------------ full-size workloads
 
 
-def _sample_rows(m, fixture_rows, n_extra, seed):
-    rng = np.random.default_rng(seed)
-    extra = rng.choice(m, size=min(n_extra, m), replace=False)
-    return np.unique(np.concatenate([fixture_rows, extra]))
+def _oracle_rows(fn, x_bits, *rest, chunk=1024):
+    """The oracle on every row of x, in row blocks (rows are independent), to bound host memory."""
+    out = [fn(f32(x_bits[r:r + chunk]), *rest) for r in range(0, x_bits.shape[0], chunk)]
+    return np.concatenate(out, axis=0)
+
+
+def _ulp_bf16(v):
+    """Spacing of the bf16 grid at |v| (normal range)."""
+    e = np.floor(np.log2(np.maximum(np.abs(v), 2.0 ** -126)))
+    return np.exp2(e - 7)
+
+
+def assert_parity_all_rows(got, golden, emulated, what, floor_budget=10, pin_abs=1e-3, max_differ=1e-2):
+    """Every element of a full-size output, three ways.
+
+    1. The kernel's arithmetic: within one bf16 ulp (plus pin_abs * rms) of the oracle's emulation of the device
+       rounding points (bf16(x * gamma) staged, fp32 accumulation, fp32 1/rms, bf16 hidden block, bf16 output),
+       and, when max_differ is given, equal to it on all but that fraction of the elements. Without a GELU they
+       differ only where the tensor cores' fp32 accumulation order (against numpy's) moves a value across a
+       bf16 rounding midpoint: measured on B200, 0.24 % of the QKV outputs, each by one ulp, plus absolute
+       noise near zero. The MLP's tanh GELU runs on the hardware tanh (relative error about 2^-11), which moves
+       some hidden-block roundings (5 % of the outputs differ, by one ulp), so its outputs get a larger
+       absolute slack and no count.
+    2. PCC >= 0.9999 against the fp32 golden.
+    3. max |y - golden| / rms(golden) <= 2e-2 on every element, except where the emulated device rounding is
+       itself at the bar: with 50M outputs, bf16 staging plus bf16 output rounding reach 2e-2 at a handful of
+       elements (QKV 8192x4096x6144: one element at 0.020015). Those are counted (at most floor_budget) and must
+       match the emulation.
+    """
+    got = np.asarray(got, dtype=np.float64)
+    emu = np.asarray(emulated, dtype=np.float64)
+    g = np.asarray(golden, dtype=np.float64)
+    assert np.array_equal(O.to_bf16(got.astype(np.float32)), got.astype(np.float32)), f"{what}: output is not bf16"
+    rms = float(np.sqrt(np.mean(g * g)))
+    d_emu = np.abs(got - emu)
+    bound = _ulp_bf16(emu) * 1.0001 + pin_abs * rms
+    assert np.all(d_emu <= bound), f"{what}: off the device numerics by {np.max(d_emu - bound):.3g} beyond 1 ulp"
+    if max_differ is not None:
+        frac = float(np.mean(d_emu > 0))
+        assert frac <= max_differ, f"{what}: {frac:.2e} of the elements differ from the device-numerics emulation"
+    m = parity(got, g)
+    assert m["pcc"] >= 0.9999, f"{what}: {m}"
+    rms = m["golden_rms"]
+    err = np.abs(got - g) / rms
+    floor = np.abs(emu - g) / rms >= 0.98 * 2e-2
+    assert int(floor.sum()) <= floor_budget, f"{what}: {int(floor.sum())} elements at the rounding floor"
+    assert np.all(err[~floor] <= 2e-2), f"{what}: max {err[~floor].max():.5f} off the floor elements"
+    assert np.all(d_emu[floor] <= bound[floor])
+    assert m["max_abs_diff"] > 0, f"{what}: output equals the fp32 golden bit for bit (vacuous)"
+    return m, int(floor.sum()), float(err.max())
 
 
 def test_qkv_full_size(ops, golden_vectors):
+    """All 8192 rows of the QKV workload against the oracle, plus the reference's own golden rows. Every output
+    tile is compared, the last, partly filled wave of the persistent kernel included (768 tiles on 74 pairs)."""
     name = "qkv_8192x4096x6144"
     t = W.generate(name)
     y = host(ops.fused_rmsnorm_matmul(dev(t["x"]), dev(t["gamma"]), dev(t["w"]), 1e-5))
     fr = golden_vectors[f"{name}/rows"]
     assert_parity(y[fr], golden_vectors[f"{name}/golden"], "qkv fixture rows")
-    rows = _sample_rows(8192, fr, 60, 1)
-    g = O.fused_rmsnorm_matmul(f32(t["x"][rows]), f32(t["gamma"]), f32(t["w"]), 1e-5)
-    assert_parity(y[rows], g, "qkv sampled rows")
+    gm, w = f32(t["gamma"]), f32(t["w"])
+    g = _oracle_rows(lambda xs: O.fused_rmsnorm_matmul(xs, gm, w, 1e-5), t["x"])
+    e = _oracle_rows(lambda xs: O.emulate_device_fused_rmsnorm_matmul(xs, gm, w, 1e-5), t["x"])
+    assert_parity_all_rows(y, g, e, "qkv all rows")
     assert np.all(np.isfinite(y))
 
 
 @pytest.mark.parametrize("name", ["mlp_8192x4096x16384", "decode_mlp_32x8192x28672"])
 def test_mlp_full_size(ops, golden_vectors, name):
+    """erf: the reference golden's rows (fixtures). tanh (the benchmark's form): every row against the oracle."""
     t = W.generate(name)
     x = dev(t["x"])
     args = (x, dev(t["gamma"]), dev(t["w1"]), dev(t["b1"]), dev(t["w2"]), x, 1e-5)
@@ -207,11 +257,73 @@ def test_mlp_full_size(ops, golden_vectors, name):
     y = host(ops.fused_mlp(*args, gelu="erf"))
     assert_parity(y[fr], golden_vectors[f"{name}/golden"], f"{name} erf fixture rows")
     yt = host(ops.fused_mlp(*args, gelu="tanh"))
-    rows = _sample_rows(t["x"].shape[0], fr, 28, 2)
-    xs = f32(t["x"][rows])
-    g = O.fused_mlp(xs, f32(t["gamma"]), f32(t["w1"]), f32(t["b1"]), f32(t["w2"]), xs, 1e-5, "tanh")
-    assert_parity(yt[rows], g, f"{name} tanh sampled rows")
+    gm, w1, b1, w2 = f32(t["gamma"]), f32(t["w1"]), f32(t["b1"]), f32(t["w2"])
+    g = _oracle_rows(lambda xs: O.fused_mlp(xs, gm, w1, b1, w2, xs, 1e-5, "tanh"), t["x"])
+    e = _oracle_rows(lambda xs: O.emulate_device_fused_mlp(xs, gm, w1, b1, w2, xs, 1e-5, "tanh"), t["x"])
+    assert_parity_all_rows(yt, g, e, f"{name} tanh all rows", pin_abs=3e-3, max_differ=None)
     assert np.all(np.isfinite(y)) and np.all(np.isfinite(yt))
+
+
+# One GPU's share of the row-sharded workloads at 2, 4 and 8 GPUs. Their GEMMs end in a partly filled wave
+# (e.g. 96 QKV tiles or 256 up-projection tiles on 74 CTA pairs), which the pair kernel may split over the idle
+# pairs with fp32 partial slots: every row is compared with the oracle, and two identical calls must agree bit
+# for bit (the slots are added in a fixed order).
+SHARDS = [1024, 2048, 4096]
+
+
+@pytest.mark.parametrize("rows", SHARDS)
+def test_qkv_row_shard(ops, rows):
+    t = W.generate("qkv_8192x4096x6144", rows=(0, rows))
+    x, gm, w = dev(t["x"]), dev(t["gamma"]), dev(t["w"])
+    y1 = ops.fused_rmsnorm_matmul(x, gm, w, 1e-5)
+    y2 = ops.fused_rmsnorm_matmul(x, gm, w, 1e-5)
+    assert torch.equal(y1, y2), "two identical calls differ"
+    gm, w = f32(t["gamma"]), f32(t["w"])
+    g = _oracle_rows(lambda xs: O.fused_rmsnorm_matmul(xs, gm, w, 1e-5), t["x"])
+    e = _oracle_rows(lambda xs: O.emulate_device_fused_rmsnorm_matmul(xs, gm, w, 1e-5), t["x"])
+    assert_parity_all_rows(host(y1), g, e, f"qkv {rows} rows")
+
+
+@pytest.mark.parametrize("rows", SHARDS)
+def test_mlp_row_shard(ops, rows):
+    t = W.generate("mlp_8192x4096x16384", rows=(0, rows))
+    x = dev(t["x"])
+    args = (x, dev(t["gamma"]), dev(t["w1"]), dev(t["b1"]), dev(t["w2"]), x, 1e-5)
+    y1 = ops.fused_mlp(*args, gelu="tanh")
+    y2 = ops.fused_mlp(*args, gelu="tanh")
+    assert torch.equal(y1, y2), "two identical calls differ"
+    gm, w1, b1, w2 = f32(t["gamma"]), f32(t["w1"]), f32(t["b1"]), f32(t["w2"])
+    g = _oracle_rows(lambda xs: O.fused_mlp(xs, gm, w1, b1, w2, xs, 1e-5, "tanh"), t["x"])
+    e = _oracle_rows(lambda xs: O.emulate_device_fused_mlp(xs, gm, w1, b1, w2, xs, 1e-5, "tanh"), t["x"])
+    assert_parity_all_rows(host(y1), g, e, f"mlp {rows} rows", pin_abs=3e-3, max_differ=None)
+
+
+def test_minimum_workspace_runs_without_the_split(ops):
+    """A workspace of the minimum size (hidden block + staging, no split region) is accepted and gives the same
+    result within the parity bar; one byte less is refused."""
+    from tfb200 import _lib as L
+
+    t = W.generate("qkv_8192x4096x6144", rows=(0, 1024))
+    x, gm, w = dev(t["x"]), dev(t["gamma"]), dev(t["w"])
+    full = ops.rmsnorm_matmul_workspace_bytes(1024, 4096, 6144)
+    minimum = 1024 * 4096 * 2 + 1024 * 4
+    assert full > minimum
+    ws = torch.empty(full, dtype=torch.uint8, device="cuda")
+    y_full = ops.fused_rmsnorm_matmul(x, gm, w, 1e-5, workspace=ws)
+    y = torch.empty_like(y_full)
+    import ctypes
+
+    lib = L.lib()
+    args = (ctypes.byref(ops.mat(x)), ctypes.c_void_p(gm.data_ptr()), ctypes.byref(ops.mat(w)), ctypes.c_float(1e-5),
+            ctypes.byref(ops.mat(y)), ctypes.c_void_p(ops.stream_ptr()), ctypes.c_void_p(ws.data_ptr()))
+    assert lib.tfb200_fused_rmsnorm_matmul(*args, ctypes.c_size_t(minimum)) == L.TFB200_OK
+    m = parity(host(y), host(y_full))
+    assert m["ok"], m
+    gm, w = f32(t["gamma"]), f32(t["w"])
+    g = O.fused_rmsnorm_matmul(f32(t["x"]), gm, w, 1e-5)
+    e = O.emulate_device_fused_rmsnorm_matmul(f32(t["x"]), gm, w, 1e-5)
+    assert_parity_all_rows(host(y), g, e, "minimum workspace")
+    assert lib.tfb200_fused_rmsnorm_matmul(*args, ctypes.c_size_t(minimum - 1)) == L.TFB200_EWORKSPACE
 
 
 def test_concurrent_calls_from_threads_on_separate_streams(ops):

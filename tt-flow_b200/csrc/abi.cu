@@ -2,6 +2,7 @@
 // reporting and dispatch to the sm_100a kernels.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstring>
 #include <mutex>
@@ -9,6 +10,7 @@
 
 #include "../../include/tfb200.h"
 #include "internal.h"
+#include "pair_sched.h"
 #include "sm100_ptx.cuh"
 
 namespace tfb200 {
@@ -76,7 +78,36 @@ bool mat_ok(const tfb200_mat* m, const char* name, std::string* err) {
 
 const bf16* as_bf16(const void* p) { return static_cast<const bf16*>(p); }
 
+// Largest dimension the size functions accept: products of three such values
+// and small constants stay far inside size_t.
+constexpr int64_t kMaxDim = int64_t(1) << 30;
+constexpr size_t kTooBig = ~size_t(0);
+
+size_t al256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+
+int64_t pair_tiles(int64_t m, int64_t n) { return ((m + 255) / 256) * ((n + 255) / 256); }
+
+// The fused MLP's tail-split region (pair_sched.h): flags of the up- and the
+// down-projection, then slots shared by both launches (the down-projection runs
+// after the up-projection has completed).
+size_t mlp_split_bytes(int64_t m, int64_t h, int64_t n) {
+  if (m <= cfg::kTileM) return 0;
+  const int64_t t = std::max(pair_tiles(m, h), pair_tiles(m, n));
+  return static_cast<size_t>(2 * sched::flag_bytes() + sched::slot_count(t) * sched::kSlotBytes);
+}
+
 }  // namespace
+
+// Workspace the fused MLP cannot run without: the bf16 hidden block and the
+// RMSNorm staging (or the streamed path's buffers for few rows). A workspace
+// of tfb200_fused_mlp_workspace_size() bytes adds the tail-split region.
+size_t mlp_workspace_min_bytes(int64_t m, int64_t k, int64_t h, int64_t n) {
+  if (m <= 0 || h <= 0 || k <= 0) return 0;
+  if (m > kMaxDim || k > kMaxDim || h > kMaxDim || n > kMaxDim) return kTooBig;
+  size_t need = al256(static_cast<size_t>(m) * static_cast<size_t>(h) * 2) + rms_prep_bytes(m, k);
+  if (m <= kStreamMaxRows && n > 0) need = std::max(need, decode_mlp_bytes(m, k, h, n));
+  return need;
+}
 
 int* device_status_ptr(std::string* err) {
   static int* ptrs[64] = {};
@@ -187,9 +218,9 @@ int tfb200_matmul(const tfb200_mat* a, const tfb200_mat* b, tfb200_mat* c, void*
 }
 
 size_t tfb200_fused_rmsnorm_matmul_workspace_size(int64_t m, int64_t k, int64_t n) {
-  (void)n;
   if (m <= 0 || k <= 0) return 0;
-  return rms_prep_bytes(m, k);
+  if (m > kMaxDim || k > kMaxDim || n > kMaxDim) return kTooBig;
+  return rms_prep_bytes(m, k) + pair_split_bytes(m, n);
 }
 
 int tfb200_fused_rmsnorm_matmul(const tfb200_mat* x, const void* gamma, const tfb200_mat* w, float eps,
@@ -203,18 +234,24 @@ int tfb200_fused_rmsnorm_matmul(const tfb200_mat* x, const void* gamma, const tf
   if (y->rows == 0 || y->cols == 0) return TFB200_OK;
   if (x->cols == 0) return fail(TFB200_EINVAL, "tfb200_fused_rmsnorm_matmul: RMSNorm over an empty dimension");
   if (!gamma) return fail(TFB200_EINVAL, "tfb200_fused_rmsnorm_matmul: null gamma");
-  const size_t need = tfb200_fused_rmsnorm_matmul_workspace_size(x->rows, x->cols, w->cols);
-  if (!workspace || workspace_bytes < need)
+  const size_t base = rms_prep_bytes(x->rows, x->cols);
+  if (!workspace || workspace_bytes < base)
     return fail(TFB200_EWORKSPACE,
-                "tfb200_fused_rmsnorm_matmul: workspace smaller than tfb200_fused_rmsnorm_matmul_workspace_size()");
+                "tfb200_fused_rmsnorm_matmul: workspace smaller than the staging block it needs "
+                "(tfb200_fused_rmsnorm_matmul_workspace_size() bytes give the fastest schedule)");
   if (reinterpret_cast<uintptr_t>(workspace) & 255u)
     return fail(TFB200_EWORKSPACE, "tfb200_fused_rmsnorm_matmul: workspace must be 256-byte aligned");
+  // With the full workspace the GEMM may split the tail of its last wave; the
+  // split's flags are cleared by the staging launch.
+  const size_t split = pair_split_bytes(x->rows, w->cols);
+  const bool use_split = split && workspace_bytes - base >= split;
+  char* sp = static_cast<char*>(workspace) + base;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   bf16* a = nullptr;
   int64_t lda = 0;
   float* inv = nullptr;
   int rc = run_rms_prep(as_bf16(x->data), x->ld, as_bf16(gamma), x->rows, x->cols, eps, workspace, &a, &lda, &inv,
-                        s, &err);
+                        s, &err, use_split ? sp : nullptr, use_split ? static_cast<size_t>(sched::flag_bytes()) : 0);
   if (rc) return fail(rc, "tfb200_fused_rmsnorm_matmul: " + err);
   GemmProblem g;
   g.M = x->rows;
@@ -227,19 +264,20 @@ int tfb200_fused_rmsnorm_matmul(const tfb200_mat* x, const void* gamma, const tf
   g.C = static_cast<bf16*>(y->data);
   g.ldc = y->ld;
   g.row_scale = inv;
+  g.b_stable = true;  // preceded by the staging pass, which writes only the workspace
+  if (use_split) {
+    g.sk_flags = reinterpret_cast<int*>(sp);
+    g.sk_slots = reinterpret_cast<float*>(sp + sched::flag_bytes());
+    g.sk_max_slots = static_cast<int>(sched::slot_count(pair_tiles(g.M, g.N)));
+  }
   rc = run_gemm(g, s, &err);
   return rc ? fail(rc, "tfb200_fused_rmsnorm_matmul: " + err) : TFB200_OK;
 }
 
 size_t tfb200_fused_mlp_workspace_size(int64_t m, int64_t k, int64_t h, int64_t n) {
-  if (m <= 0 || h <= 0 || k <= 0) return 0;
-  const size_t hid = (static_cast<size_t>(m) * static_cast<size_t>(h) * 2 + 255) & ~static_cast<size_t>(255);
-  size_t need = hid + rms_prep_bytes(m, k);
-  if (m <= kStreamMaxRows && n > 0) {
-    const size_t d = decode_mlp_bytes(m, k, h, n);
-    if (d > need) need = d;
-  }
-  return need;
+  const size_t base = mlp_workspace_min_bytes(m, k, h, n);
+  if (base == 0 || base == kTooBig) return base;
+  return base + mlp_split_bytes(m, h, n);
 }
 
 int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w1, const void* b1,
@@ -261,9 +299,11 @@ int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w
   if (K == 0) return fail(TFB200_EINVAL, "tfb200_fused_mlp: RMSNorm over an empty dimension");
   if (!gamma) return fail(TFB200_EINVAL, "tfb200_fused_mlp: null gamma");
   if (H == 0) return fail(TFB200_EUNSUPPORTED, "tfb200_fused_mlp: empty hidden dimension");
-  const size_t need = tfb200_fused_mlp_workspace_size(M, K, H, N);
+  const size_t need = mlp_workspace_min_bytes(M, K, H, N);
   if (!workspace || workspace_bytes < need)
-    return fail(TFB200_EWORKSPACE, "tfb200_fused_mlp: workspace smaller than tfb200_fused_mlp_workspace_size()");
+    return fail(TFB200_EWORKSPACE,
+                "tfb200_fused_mlp: workspace smaller than the hidden block and staging it needs "
+                "(tfb200_fused_mlp_workspace_size() bytes give the fastest schedule)");
   if (reinterpret_cast<uintptr_t>(workspace) & 255u)
     return fail(TFB200_EWORKSPACE, "tfb200_fused_mlp: workspace must be 256-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -276,12 +316,19 @@ int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w
     return rc ? fail(rc, "tfb200_fused_mlp (streamed): " + err) : TFB200_OK;
   }
   bf16* hid = static_cast<bf16*>(workspace);
-  const size_t hid_bytes = (static_cast<size_t>(M) * static_cast<size_t>(H) * 2 + 255) & ~static_cast<size_t>(255);
+  const size_t hid_bytes = al256(static_cast<size_t>(M) * static_cast<size_t>(H) * 2);
+  const size_t base = hid_bytes + rms_prep_bytes(M, K);
+  // With the full workspace both GEMMs may split the tail of their last wave;
+  // the split's flags are cleared by the staging launch.
+  const size_t split = mlp_split_bytes(M, H, N);
+  const bool use_split = split && workspace_bytes >= base && workspace_bytes - base >= split;
+  char* sp = static_cast<char*>(workspace) + base;
   bf16* a = nullptr;
   int64_t lda = 0;
   float* inv = nullptr;
   int rc = run_rms_prep(as_bf16(x->data), x->ld, as_bf16(gamma), M, K, eps, static_cast<char*>(workspace) + hid_bytes,
-                        &a, &lda, &inv, s, &err);
+                        &a, &lda, &inv, s, &err, use_split ? sp : nullptr,
+                        use_split ? static_cast<size_t>(2 * sched::flag_bytes()) : 0);
   if (rc) return fail(rc, "tfb200_fused_mlp: " + err);
   GemmProblem g1;
   g1.M = M;
@@ -296,6 +343,13 @@ int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w
   g1.row_scale = inv;
   g1.bias = as_bf16(b1);
   g1.gelu = gelu_mode == TFB200_GELU_ERF ? kGeluErf : kGeluTanh;
+  float* slots = reinterpret_cast<float*>(sp + 2 * sched::flag_bytes());
+  g1.b_stable = true;  // preceded by the staging pass, which writes only the workspace
+  if (use_split) {
+    g1.sk_flags = reinterpret_cast<int*>(sp);
+    g1.sk_slots = slots;
+    g1.sk_max_slots = static_cast<int>(sched::slot_count(pair_tiles(M, H)));
+  }
   rc = run_gemm(g1, s, &err);
   if (rc) return fail(rc, "tfb200_fused_mlp (up projection): " + err);
   GemmProblem g2;
@@ -310,6 +364,12 @@ int tfb200_fused_mlp(const tfb200_mat* x, const void* gamma, const tfb200_mat* w
   g2.ldc = y->ld;
   g2.residual = as_bf16(residual->data);
   g2.ldr = residual->ld;
+  g2.b_stable = true;  // preceded by the up-projection, which writes only the hidden block
+  if (use_split) {
+    g2.sk_flags = reinterpret_cast<int*>(sp + sched::flag_bytes());
+    g2.sk_slots = slots;
+    g2.sk_max_slots = static_cast<int>(sched::slot_count(pair_tiles(M, N)));
+  }
   rc = run_gemm(g2, s, &err);
   if (rc) return fail(rc, "tfb200_fused_mlp (down projection): " + err);
   return TFB200_OK;

@@ -38,6 +38,7 @@
 
 #include "internal.h"
 #include "kernel_config.h"
+#include "pair_sched.h"
 #include "sm100_ptx.cuh"
 
 namespace tfb200 {
@@ -70,6 +71,15 @@ struct KParams {
   int tma_store;  // the pair kernel stores C through shared memory with TMA
   int* status;
   uint64_t timeout_ns;
+  // CTA-pair kernel only: the work schedule (pair_sched.h) and, for its tail
+  // split, the caller's slots (fp32 partial accumulators) and their flags.
+  sched::PairSched ps;
+  float* sk_slots;
+  int* sk_flags;
+  // The preceding kernel in the stream does not write B (the fused paths, where
+  // it is this library's staging pass or up-projection): the pair kernel may
+  // request its first stages of B before waiting for that kernel.
+  int b_prefetch;
 };
 
 struct SmemCtl {
@@ -494,8 +504,11 @@ struct PairCtl {
 };
 
 // Epilogue staging for TMA stores: per epilogue warp two 32 x 32 bf16 buffers.
+constexpr int PEPI = cfg::kPairEpiWarps;  // epilogue warps 4 .. 4 + PEPI - 1
+constexpr int PCHUNKS = BN / 32 / (PEPI / 4);  // 32-column chunks per epilogue warp
 constexpr uint32_t C_STAGE_BYTES = 32 * 32 * 2;
-constexpr uint32_t C_STAGING_BYTES = 4 * 2 * C_STAGE_BYTES;
+constexpr uint32_t C_STAGING_BYTES = PEPI * 2 * C_STAGE_BYTES;
+static_assert(PEPI == 8 && PCHUNKS == 4, "two epilogue warps per TMEM lane quadrant");
 static_assert(C_STAGING_BYTES == cfg::kPairStagingBytes, "planner's epilogue staging size");
 static_assert(sizeof(PairCtl) == cfg::kPairCtlBytes, "planner's pair control-block size");
 static_assert(PBM == cfg::kPairTileM, "planner's pair tile");
@@ -511,7 +524,7 @@ __device__ __forceinline__ void raise_abort_pair(PairCtl* ctl, int* status) {
 
 // GROUP: raster group (row tiles) of the pair tiles; see launch_pair.
 template <int GROUP>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(cfg::kPairThreads, 1)
     k_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const KParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -534,7 +547,7 @@ __global__ void __launch_bounds__(256, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&ctl->tfull[b]), 1);
-      mbar_init(smem_u32(&ctl->tempty[b]), 8);  // 4 epilogue warps in each CTA
+      mbar_init(smem_u32(&ctl->tempty[b]), 2 * PEPI);  // the epilogue warps of both CTAs
     }
     mbar_init(smem_u32(&ctl->drain), 1);
     ctl->abort = 0;
@@ -555,14 +568,13 @@ __global__ void __launch_bounds__(256, 1)
   // as this grid's CTAs exit (its prologue overlaps this grid's tail); this grid
   // touches no global memory before the preceding grid has completed.
   grid_dep_launch();
-  grid_dep_wait();
+  if (warp != 0) grid_dep_wait();  // the producer waits below, after its weight prefetch
 
   const int pair = blockIdx.x >> 1;
-  const int npairs = gridDim.x >> 1;
+  const sched::PairSched& ps = p.ps;  // ps.pairs == gridDim.x / 2 (the launcher sets it)
+  const int nwork = sched::work_count(ps, pair);
   const int num_m = (p.M + PBM - 1) / PBM;
   const int num_n = (p.N + BN - 1) / BN;
-  const int total = num_m * num_n;
-  const int kblocks = (p.K + BK - 1) / BK;
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer (both CTAs)
@@ -570,23 +582,48 @@ __global__ void __launch_bounds__(256, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = pair; t < total && ok; t += npairs) {
+      // Weight prefetch: the first item's first stages of B (which the preceding
+      // kernel does not write) are requested while that kernel finishes; their
+      // stages are armed for A and B now, and A follows after the wait. The
+      // stages are fresh, so no `empty` wait precedes them.
+      int npre = 0;
+      if (p.b_prefetch && nwork > 0) {
+        const sched::Work w = sched::work_item(ps, pair, 0);
         int tm, tn;
-        tile_coords_g<GROUP>(t, num_m, num_n, tm, tn);
-        for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(smem_u32(&ctl->empty[stage]), phase ^ 1u, &ctl->abort, p.timeout_ns)) {
+        tile_coords_g<GROUP>(w.tile, num_m, num_n, tm, tn);
+        npre = min(PSTAGES, w.k1 - w.k0);
+        for (int s = 0; s < npre; ++s) {
+          const uint32_t fb = mapa_shared(smem_u32(&ctl->full[s]), 0);
+          if (leader) mbar_arrive_expect_tx(smem_u32(&ctl->full[s]), 2 * (A_STAGE_BYTES + PB_STAGE_BYTES));
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            tma_load_2d_pair(smem_u32(sB + s * PB_STAGE_BYTES + j * 8192), &tmB, fb,
+                             tn * BN + static_cast<int>(rank) * 128 + j * 64, (w.k0 + s) * BK);
+        }
+      }
+      grid_dep_wait();
+      for (int i = 0; i < nwork && ok; ++i) {
+        const sched::Work w = sched::work_item(ps, pair, i);
+        int tm, tn;
+        tile_coords_g<GROUP>(w.tile, num_m, num_n, tm, tn);
+        for (int kb = w.k0; kb < w.k1; ++kb) {
+          const bool pre = i == 0 && kb - w.k0 < npre;  // armed, B in flight
+          if (!pre && !mbar_wait(smem_u32(&ctl->empty[stage]), phase ^ 1u, &ctl->abort, p.timeout_ns)) {
             raise_abort_pair(ctl, p.status);
             ok = false;
             break;
           }
           const uint32_t fb = mapa_shared(smem_u32(&ctl->full[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(smem_u32(&ctl->full[stage]), 2 * (A_STAGE_BYTES + PB_STAGE_BYTES));
+          if (leader && !pre)
+            mbar_arrive_expect_tx(smem_u32(&ctl->full[stage]), 2 * (A_STAGE_BYTES + PB_STAGE_BYTES));
           tma_load_2d_pair(smem_u32(sA + stage * A_STAGE_BYTES), &tmA, fb, kb * BK,
                            tm * PBM + static_cast<int>(rank) * BM);
+          if (!pre) {
 #pragma unroll
-          for (int j = 0; j < 2; ++j)
-            tma_load_2d_pair(smem_u32(sB + stage * PB_STAGE_BYTES + j * 8192), &tmB, fb,
-                             tn * BN + static_cast<int>(rank) * 128 + j * 64, kb * BK);
+            for (int j = 0; j < 2; ++j)
+              tma_load_2d_pair(smem_u32(sB + stage * PB_STAGE_BYTES + j * 8192), &tmB, fb,
+                               tn * BN + static_cast<int>(rank) * 128 + j * 64, kb * BK);
+          }
           if (++stage == PSTAGES) {
             stage = 0;
             phase ^= 1u;
@@ -608,8 +645,8 @@ __global__ void __launch_bounds__(256, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      int i = 0;
-      for (int t = pair; t < total && ok; t += npairs, ++i) {
+      for (int i = 0; i < nwork && ok; ++i) {
+        const sched::Work w = sched::work_item(ps, pair, i);
         const int acc = i & 1;
         const uint32_t use = static_cast<uint32_t>(i >> 1);
         if (!mbar_wait(smem_u32(&ctl->tempty[acc]), (use & 1u) ^ 1u, &ctl->abort, p.timeout_ns)) {
@@ -619,7 +656,7 @@ __global__ void __launch_bounds__(256, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < kblocks && ok; ++kb) {
+        for (int kb = w.k0; kb < w.k1 && ok; ++kb) {
           if (!mbar_wait(smem_u32(&ctl->full[stage]), phase, &ctl->abort, p.timeout_ns)) {
             raise_abort_pair(ctl, p.status);
             ok = false;
@@ -632,7 +669,7 @@ __global__ void __launch_bounds__(256, 1)
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
             const uint64_t bd = sdesc_sw128(b0 + k * 2048, 8192, 1024);
-            mma_bf16_pair(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            mma_bf16_pair(d, ad, bd, idesc, (kb != w.k0 || k != 0) ? 1u : 0u);
           }
           mma_commit_pair_both(smem_u32(&ctl->empty[stage]), 0x3);
           if (++stage == PSTAGES) {
@@ -651,12 +688,16 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------- epilogue (both CTAs)
+    // Warp w reads TMEM lane quadrant q = w % 4 (rows q*32 .. q*32+31 of this
+    // CTA's 128) and the column chunks [c0, c0 + PCHUNKS) of the tile.
     const int q = warp & 3;
+    const int ew = warp - 4;                 // epilogue warp 0 .. PEPI-1
+    const int c0 = (ew >> 2) * PCHUNKS;      // first of this warp's 32-column chunks
     const int r = q * 32 + lane;
-    int i = 0;
-    for (int t = pair; t < total; t += npairs, ++i) {
+    for (int i = 0; i < nwork; ++i) {
+      const sched::Work w = sched::work_item(ps, pair, i);
       int tm, tn;
-      tile_coords_g<GROUP>(t, num_m, num_n, tm, tn);
+      tile_coords_g<GROUP>(w.tile, num_m, num_n, tm, tn);
       const int acc = i & 1;
       const uint32_t use = static_cast<uint32_t>(i >> 1);
       bool ok = mbar_wait(smem_u32(&ctl->tfull[acc]), use & 1u, &ctl->abort, p.timeout_ns);
@@ -668,14 +709,87 @@ __global__ void __launch_bounds__(256, 1)
       tc_fence_after();
       const int64_t row0 = static_cast<int64_t>(tm) * PBM + static_cast<int64_t>(rank) * BM + q * 32;
       const int64_t row = row0 + lane;
+      const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      if (w.role == sched::kPart) {
+        // Helper part of a split tile: this warp's 32 rows of the fp32
+        // accumulator go to the part's slot (layout [chunk][column / 4][row][4],
+        // so each warp-wide 16-byte store covers 512 contiguous bytes), then the
+        // warp's flag is raised. Warps whose rows are all past the matrix skip
+        // both, as the main pair's matching warp skips the wait.
+        if (row0 < p.M) {
+          float4* slot = reinterpret_cast<float4*>(p.sk_slots + (static_cast<int64_t>(w.slot) * 2 + rank) * (BM * BN)) + r;
+          int* flag = p.sk_flags + ((w.slot * 2 + static_cast<int>(rank)) * PEPI + ew) * PCHUNKS;
+          for (int c = c0; c < c0 + PCHUNKS; ++c) {
+            if (tn * BN + c * 32 >= p.N) break;  // warp-uniform
+            uint32_t v[32];
+            tmem_ld_32cols(tacc + static_cast<uint32_t>(c * 32), v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4)
+              __stcg(slot + (c * 8 + j4) * BM, make_float4(__uint_as_float(v[4 * j4]), __uint_as_float(v[4 * j4 + 1]),
+                                                          __uint_as_float(v[4 * j4 + 2]),
+                                                          __uint_as_float(v[4 * j4 + 3])));
+            // Each lane publishes its row of the chunk: the chunk's counter
+            // reaches 32 once every row is in L2 (release covers the lane's stores).
+            red_add_release_gpu(flag + (c - c0), 1);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          const uint32_t te = smem_u32(&ctl->tempty[acc]);
+          if (leader)
+            mbar_arrive(te);
+          else
+            mbar_arrive_cluster(mapa_shared(te, 0));
+        }
+        continue;
+      }
+      const bool fix = w.role == sched::kMain && row0 < p.M;
+      bool fix_ok = true;
       const float scale = (p.row_scale && row < p.M) ? __ldg(p.row_scale + row) : 1.0f;
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = c0; c < c0 + PCHUNKS; ++c) {
         const int col0 = tn * BN + c * 32;
         if (col0 >= p.N || row0 >= p.M) break;  // warp-uniform: nothing of this block is in the matrix
         uint32_t v[32];
-        tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + c * 32),
-                       v);
+        tmem_ld_32cols(tacc + static_cast<uint32_t>(c * 32), v);
         tmem_wait_ld();
+        if (fix) {
+          // Own k-blocks [0, kc) first, then the parts in k order: a fixed order.
+          // Each lane waits for its row of the part's chunk (the helper lane that
+          // wrote it released the chunk's counter).
+          for (int j = 0; j < ps.parts && fix_ok; ++j) {
+            const int* f = p.sk_flags + (((w.slot + j) * 2 + static_cast<int>(rank)) * PEPI + ew) * PCHUNKS + (c - c0);
+            if (ld_acquire_gpu(f) != 32) {
+              const uint64_t t0 = global_ns();
+              while (ld_acquire_gpu(f) != 32) {
+                if (ctl->abort || global_ns() - t0 > p.timeout_ns) {
+                  fix_ok = false;
+                  break;
+                }
+              }
+            }
+            if (!__all_sync(0xffffffffu, fix_ok)) {
+              fix_ok = false;
+              break;
+            }
+            const float4* slot =
+                reinterpret_cast<const float4*>(p.sk_slots + (static_cast<int64_t>(w.slot + j) * 2 + rank) * (BM * BN)) +
+                r + c * 8 * BM;
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 a = __ldcg(slot + j4 * BM);
+              v[4 * j4] = __float_as_uint(__uint_as_float(v[4 * j4]) + a.x);
+              v[4 * j4 + 1] = __float_as_uint(__uint_as_float(v[4 * j4 + 1]) + a.y);
+              v[4 * j4 + 2] = __float_as_uint(__uint_as_float(v[4 * j4 + 2]) + a.z);
+              v[4 * j4 + 3] = __float_as_uint(__uint_as_float(v[4 * j4 + 3]) + a.w);
+            }
+          }
+          if (!fix_ok) {
+            if (lane == 0) raise_abort_pair(ctl, p.status);
+            break;
+          }
+        }
         if (!p.tma_store) {
           if (row < p.M) epilogue_chunk(p, v, scale, row, col0);
           continue;
@@ -692,7 +806,7 @@ __global__ void __launch_bounds__(256, 1)
         }
         if (lane == 0) bulk_wait_read<1>();  // the store that used this buffer has read it
         __syncwarp();
-        const uint32_t buf = smem_u32(sC) + static_cast<uint32_t>((q * 2 + (c & 1)) * C_STAGE_BYTES);
+        const uint32_t buf = smem_u32(sC) + static_cast<uint32_t>((ew * 2 + (c & 1)) * C_STAGE_BYTES);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const uint32_t a = buf + static_cast<uint32_t>(lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4));
@@ -708,6 +822,15 @@ __global__ void __launch_bounds__(256, 1)
           bulk_commit();
         }
       }
+      if (!fix_ok) break;
+      if (fix) {
+        // The parts are consumed: return the counters to zero for the next launch.
+        __syncwarp();
+        if (lane < ps.parts * PCHUNKS)
+          st_relaxed_gpu(p.sk_flags + (((w.slot + lane / PCHUNKS) * 2 + static_cast<int>(rank)) * PEPI + ew) * PCHUNKS +
+                             lane % PCHUNKS,
+                         0);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -719,7 +842,6 @@ __global__ void __launch_bounds__(256, 1)
       }
     }
   }
-
   if (warp >= 4 && lane == 0 && p.tma_store) bulk_wait_all();  // staged stores have left shared memory
   tc_fence_before();
   __syncthreads();
@@ -775,6 +897,20 @@ bool make_map_box(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, 
 
 namespace {
 
+// The pair kernel splits the tail of its last wave (pair_sched.h) when the
+// caller's workspace holds the slots and the split shortens the busiest pair's
+// work by at least 2 %. TFB200_GEMM_SCHED=dp turns the split off, =split takes
+// it for any gain (both for measurements).
+int split_min_gain_permille() {
+  static const int v = [] {  // initialised once, thread-safe
+    const char* e = std::getenv("TFB200_GEMM_SCHED");
+    if (e && std::string(e) == "dp") return -1;
+    if (e && std::string(e) == "split") return 0;
+    return 20;
+  }();
+  return v;
+}
+
 template <bool MANUAL>
 int launch(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int grid, cudaStream_t s,
            std::string* err) {
@@ -807,8 +943,8 @@ int launch(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int 
 }
 
 template <int GROUP>
-int launch_pair_g(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
-                  int pair_tiles, cudaStream_t s, std::string* err) {
+int launch_pair_g(const KParams& kp_in, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                  int pair_tiles, int max_slots, cudaStream_t s, std::string* err) {
   const auto kern = k_gemm_pair<GROUP>;
   // Per-device first-call setup; calls may come from several host threads.
   static std::mutex mu;
@@ -834,7 +970,7 @@ int launch_pair_g(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& t
     // Persistent pairs: launch no more clusters than can be resident at once.
     cudaLaunchConfig_t q{};
     q.gridDim = dim3(static_cast<unsigned>(sm_count()), 1, 1);
-    q.blockDim = dim3(256, 1, 1);
+    q.blockDim = dim3(cfg::kPairThreads, 1, 1);
     q.dynamicSmemBytes = smem;
     cudaLaunchAttribute qa[1];
     qa[0].id = cudaLaunchAttributeClusterDimension;
@@ -853,10 +989,20 @@ int launch_pair_g(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& t
     ready[dev].store(true, std::memory_order_release);
   }
   if (lock.owns_lock()) lock.unlock();
-  const int pairs = pair_tiles < max_clusters[dev] ? pair_tiles : max_clusters[dev];
+  // The tail split is planned over every resident pair (the helpers are the
+  // pairs a short last wave leaves idle); without it, no more pairs than tiles.
+  KParams kp = kp_in;
+  const int kblocks = (kp.K + BK - 1) / BK;
+  const int gain = split_min_gain_permille();
+  kp.ps = sched::plan(pair_tiles, kblocks, max_clusters[dev], gain >= 0 ? max_slots : 0, gain >= 0 ? gain : 0);
+  if (kp.ps.rem == 0) {
+    const int used = pair_tiles < max_clusters[dev] ? pair_tiles : max_clusters[dev];
+    kp.ps = sched::plan(pair_tiles, kblocks, used, 0);
+  }
+  const int pairs = kp.ps.pairs;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(256, 1, 1);
+  cfg.blockDim = dim3(cfg::kPairThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
@@ -883,9 +1029,9 @@ int launch_pair_g(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& t
 // 8 ran the 8192x16384x4096 down-projection 1.1 % faster; the 8192x4096x16384
 // up-projection keeps 16.
 int launch_pair(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
-                int pair_tiles, cudaStream_t s, std::string* err) {
-  return kp.K >= 8192 ? launch_pair_g<8>(kp, ta, tb, tc, pair_tiles, s, err)
-                      : launch_pair_g<GROUP_M>(kp, ta, tb, tc, pair_tiles, s, err);
+                int pair_tiles, int max_slots, cudaStream_t s, std::string* err) {
+  return kp.K >= 8192 ? launch_pair_g<8>(kp, ta, tb, tc, pair_tiles, max_slots, s, err)
+                      : launch_pair_g<GROUP_M>(kp, ta, tb, tc, pair_tiles, max_slots, s, err);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -957,11 +1103,24 @@ int run_gemm(const GemmProblem& g, cudaStream_t stream, std::string* err) {
       CUtensorMap tc{};
       kp.tma_store = aligned16(g.C) && g.ldc % 8 == 0 && tma_store_enabled();
       if (kp.tma_store && !make_map_box(&tc, g.C, g.M, g.N, g.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B, err)) return -3;
-      return launch_pair(kp, ta, tb, tc, pair_tiles, stream, err);
+      kp.b_prefetch = g.b_stable ? 1 : 0;
+      int max_slots = 0;
+      if (g.sk_slots && g.sk_flags && g.sk_max_slots > 0) {
+        kp.sk_slots = g.sk_slots;
+        kp.sk_flags = g.sk_flags;
+        max_slots = g.sk_max_slots;
+      }
+      return launch_pair(kp, ta, tb, tc, pair_tiles, max_slots, stream, err);
     }
     return launch<false>(kp, ta, tb, grid, stream, err);
   }
   return launch<true>(kp, ta, tb, grid, stream, err);
+}
+
+size_t pair_split_bytes(int64_t m, int64_t n) {
+  if (m <= BM || n <= 0) return 0;
+  const int64_t tiles = ((m + PBM - 1) / PBM) * ((n + BN - 1) / BN);
+  return static_cast<size_t>(sched::region_bytes(tiles));
 }
 
 }  // namespace tfb200

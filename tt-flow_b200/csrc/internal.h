@@ -35,6 +35,17 @@ struct GemmProblem {
   int gelu = kGeluNone;
   const bf16* residual = nullptr;
   int64_t ldr = 0;
+  // Tail split of the CTA-pair kernel's last wave (pair_sched.h): slots for
+  // up to sk_max_slots fp32 partial accumulators and their flags (zero on
+  // entry; the kernel returns them to zero). sk_max_slots = 0: no split.
+  float* sk_slots = nullptr;
+  int* sk_flags = nullptr;
+  int sk_max_slots = 0;
+  // B is not written by the kernel that precedes this GEMM in the stream (true
+  // in the fused paths, where that kernel is the library's own staging pass or
+  // up-projection): the pair kernel then requests its first stages of B before
+  // it waits for that kernel to complete.
+  bool b_stable = false;
 };
 
 // Launch the persistent tcgen05 GEMM. Returns 0 or a negative TFB200_E* code with
@@ -119,6 +130,14 @@ size_t rms_prep_bytes(int64_t m, int64_t k);
 int run_rms_prep(const bf16* x, int64_t ldx, const bf16* gamma, int64_t M, int64_t K, float eps, void* ws,
                  bf16** a_out, int64_t* lda_out, float** inv_out, cudaStream_t stream, std::string* err,
                  void* zero = nullptr, size_t zero_bytes = 0);
+
+// Minimum workspace of tfb200_fused_mlp (without the tail-split region).
+size_t mlp_workspace_min_bytes(int64_t m, int64_t k, int64_t h, int64_t n);
+
+// Workspace region of the pair kernel's tail split for a GEMM of M x N output:
+// 0 when the pair kernel does not run (M <= 128). Laid out as
+// [flags: sched::flag_bytes()][slots], 256-byte aligned.
+size_t pair_split_bytes(int64_t m, int64_t n);
 
 // Device status word (per device): set by kernels whose bounded waits ran out.
 int* device_status_ptr(std::string* err);

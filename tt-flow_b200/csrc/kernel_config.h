@@ -13,9 +13,12 @@ constexpr int kTileM = 128, kTileN = 256, kTileK = 64, kStages = 4;
 constexpr int kGemmCtlBytes = 112;  // k_gemm's barriers, TMEM address and abort flag
 
 // CTA pair (k_gemm_pair, more than 128 rows): 256 x 256 tiles per pair of CTAs
-// (cta_group::2), 6 stages of 16 KiB A + 16 KiB B per CTA, epilogue staging of
-// two 32 x 32 bf16 buffers per epilogue warp (4 warps).
-constexpr int kPairTileM = 2 * kTileM, kPairStages = 6, kPairStagingBytes = 4 * 2 * 32 * 32 * 2;
+// (cta_group::2), 6 stages of 16 KiB A + 16 KiB B per CTA, 8 epilogue warps
+// (two per TMEM lane quadrant, each taking half of the tile's columns) with
+// two 32 x 32 bf16 staging buffers each.
+constexpr int kPairEpiWarps = 8;
+constexpr int kPairThreads = (4 + kPairEpiWarps) * 32;
+constexpr int kPairTileM = 2 * kTileM, kPairStages = 6, kPairStagingBytes = kPairEpiWarps * 2 * 32 * 32 * 2;
 constexpr int kPairCtlBytes = 144;
 constexpr int kGroupM = 16;  // raster group of both tiled kernels (row tiles)
 

@@ -24,16 +24,26 @@ namespace {
 
 constexpr int kWarps = 8;
 
+// Clears `n` 16-byte words at `zero` with all threads of the grid (the flags of
+// the GEMM that follows; a few KiB).
+__device__ __forceinline__ void clear_words(uint4* __restrict__ zero, int64_t n) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+    zero[i] = make_uint4(0u, 0u, 0u, 0u);
+}
+
 template <bool VEC>
 __global__ void __launch_bounds__(kWarps * 32) k_rms_prep(const bf16* __restrict__ x, int64_t ldx,
                                                           const bf16* __restrict__ gamma, int M, int K, float eps,
                                                           bf16* __restrict__ a, int64_t lda,
-                                                          float* __restrict__ inv) {
+                                                          float* __restrict__ inv, uint4* __restrict__ zero,
+                                                          int64_t zero_vecs) {
   // Launched with programmatic serialization: wait for the preceding grid (which
   // may still read `a` or write `x`), then let the GEMM that follows place its
   // CTAs and run its prologue beside this pass's last CTAs.
   grid_dep_wait();
   grid_dep_launch();
+  clear_words(zero, zero_vecs);
   const int lane = threadIdx.x & 31;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5); row < M; row += stride) {
@@ -88,9 +98,11 @@ constexpr int kRegChunks = 16;
 __global__ void __launch_bounds__(kWarps * 32) k_rms_prep_reg(const bf16* __restrict__ x, int64_t ldx,
                                                               const bf16* __restrict__ gamma, int M, int K, float eps,
                                                               bf16* __restrict__ a, int64_t lda,
-                                                              float* __restrict__ inv) {
+                                                              float* __restrict__ inv, uint4* __restrict__ zero,
+                                                              int64_t zero_vecs) {
   grid_dep_wait();
   grid_dep_launch();
+  clear_words(zero, zero_vecs);
   const int lane = threadIdx.x & 31;
   const int nchunk = K / 8;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
@@ -231,13 +243,17 @@ int run_rms_prep(const bf16* x, int64_t ldx, const bf16* gamma, int64_t M, int64
     count_launch();
     return 0;
   }
-  if (zero_bytes) {
+  int64_t zvec = 0;
+  if (zero_bytes && (zero_bytes % 16) == 0 && al16(zero) && zero_bytes <= (1u << 20)) {
+    zvec = static_cast<int64_t>(zero_bytes / 16);  // small regions: cleared by the staging kernel itself
+  } else if (zero_bytes) {
     const cudaError_t e = cudaMemsetAsync(zero, 0, zero_bytes, stream);
     if (e != cudaSuccess) {
       if (err) *err = std::string("accumulator clear: ") + cudaGetErrorString(e);
       return -3;
     }
   }
+  uint4* zw = zvec ? static_cast<uint4*>(zero) : nullptr;
   const int64_t blocks64 = (M + kWarps - 1) / kWarps;
   const int blocks = static_cast<int>(blocks64 < 65535 * 8 ? blocks64 : 65535 * 8);
   cudaLaunchConfig_t cfg{};
@@ -251,9 +267,10 @@ int run_rms_prep(const bf16* x, int64_t ldx, const bf16* gamma, int64_t M, int64
   cfg.numAttrs = 1;
   const int Mi = static_cast<int>(M), Ki = static_cast<int>(K);
   cudaError_t e = vec && K <= kRegChunks * 32 * 8
-                      ? cudaLaunchKernelEx(&cfg, k_rms_prep_reg, x, ldx, gamma, Mi, Ki, eps, a, lda, inv)
-                  : vec ? cudaLaunchKernelEx(&cfg, k_rms_prep<true>, x, ldx, gamma, Mi, Ki, eps, a, lda, inv)
-                        : cudaLaunchKernelEx(&cfg, k_rms_prep<false>, x, ldx, gamma, Mi, Ki, eps, a, lda, inv);
+                      ? cudaLaunchKernelEx(&cfg, k_rms_prep_reg, x, ldx, gamma, Mi, Ki, eps, a, lda, inv, zw, zvec)
+                  : vec ? cudaLaunchKernelEx(&cfg, k_rms_prep<true>, x, ldx, gamma, Mi, Ki, eps, a, lda, inv, zw, zvec)
+                        : cudaLaunchKernelEx(&cfg, k_rms_prep<false>, x, ldx, gamma, Mi, Ki, eps, a, lda, inv, zw,
+                                             zvec);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     if (err) *err = std::string("rmsnorm staging launch: ") + cudaGetErrorString(e);

@@ -107,6 +107,22 @@ __device__ __forceinline__ void st_relaxed_sys(unsigned* ptr, unsigned v) {
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
 
+// Flag word handshake between CTAs of one GPU (gpu scope).
+__device__ __forceinline__ void st_release_gpu(int* ptr, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_gpu(int* ptr, int v) {
+  asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_add_release_gpu(int* ptr, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
 // fp32 load with system-scope relaxed semantics (another GPU may have written it).
 __device__ __forceinline__ float ld_relaxed_sys(const float* ptr) {
   float v;
