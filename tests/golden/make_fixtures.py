@@ -3,7 +3,7 @@
 Run in a container that has the tensixflow sources (the reference's Python
 package is imported unmodified from ``<reference>/python``):
 
-    python tests/golden/make_fixtures.py --reference /root/reference
+    python tests/golden/make_fixtures.py --reference <tt-flow source tree>
 
 It writes ``golden_vectors.npz`` holding, for every workload:
 
@@ -24,6 +24,7 @@ Nothing on the GPU box reads the reference: the tests only read these files.
 from __future__ import annotations
 
 import argparse
+import os
 import hashlib
 import sys
 from pathlib import Path
@@ -51,8 +52,11 @@ def sha(a: np.ndarray) -> str:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("TENSIXFLOW_REFERENCE"),
+                    help="root of a tt-flow source tree (default: $TENSIXFLOW_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the tt-flow source tree with --reference or TENSIXFLOW_REFERENCE")
     sys.path.insert(0, str(Path(args.reference) / "python"))
     from tensixflow import golden as G  # the reference, unmodified
     from tensixflow import rounding as R

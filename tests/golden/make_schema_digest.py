@@ -1,6 +1,6 @@
 """Derive tests/golden/plan_schema_digest.json from the reference's plan schema.
 
-    python tests/golden/make_schema_digest.py --reference /root/reference
+    python tests/golden/make_schema_digest.py --reference <tt-flow source tree>
 
 The digest keeps, for every object in tensixflow's schema/plan.schema.json, its
 required keys, whether extra keys are allowed, and each property's JSON type
@@ -10,6 +10,7 @@ reference at test time.
 """
 
 import argparse
+import os
 import json
 from pathlib import Path
 
@@ -29,8 +30,11 @@ def digest(node):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("TENSIXFLOW_REFERENCE"),
+                    help="root of a tt-flow source tree (default: $TENSIXFLOW_REFERENCE)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("name the tt-flow source tree with --reference or TENSIXFLOW_REFERENCE")
     schema = json.loads((Path(a.reference) / "schema" / "plan.schema.json").read_text())
     out = Path(__file__).resolve().parent / "plan_schema_digest.json"
     out.write_text(json.dumps(digest(schema), indent=1, sort_keys=True) + "\n")
