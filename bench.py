@@ -11,7 +11,9 @@ is fixed, `value` is the whole job's TFLOP/s); `--scaling weak` gives every
 rank its own 8192 rows instead. `--shard-of N` times, on one GPU, the share
 one rank has in an N-way split. Timing: W untimed warm-up steps,
 then exactly K steps between barrier + synchronize pairs, CUDA events on the
-launching stream, max over ranks. Inputs (W1 + W2 + X = 320 MiB) exceed the
+launching stream, max over ranks; the timed steps replay one step recorded in
+a CUDA graph (`--eager`: the public call per step). `e2e` always runs the
+public call with host buffers. Inputs (W1 + W2 + X = 320 MiB) exceed the
 126 MB L2, so no flush is needed between steps.
 
 ``--impl reference`` times the reference's CPU algorithm instead (the oracle's
@@ -451,23 +453,44 @@ def run_ours(args) -> int:
         step()
     barrier()
     torch.cuda.synchronize()
+    # The timed loop replays one step recorded in a CUDA graph, as a serving loop runs a fixed-shape step: the
+    # same kernels and arguments as the eager call, without the host's per-call work (argument checks, tensor
+    # maps, three launches: about 54 us per call, which eight ranks sharing the host's cores do not all hide
+    # behind a 200 us step). `--eager` times the public call itself. The path with an NCCL all-reduce stays
+    # eager.
+    graph = None
+    timed = step
+    launches_per_replay = 0
+    if not args.eager and not (tp and world > 1 and not fused_tp):
+        graph = torch.cuda.CUDAGraph()
+        lc = lib.tfb200_launch_count()
+        with torch.cuda.graph(graph):
+            step()
+        launches_per_replay = lib.tfb200_launch_count() - lc
+        timed = graph.replay
+        for _ in range(2):
+            timed()
+        torch.cuda.synchronize()
+        barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     l0 = lib.tfb200_launch_count()
     w0 = time.time()
     e0.record()
     for _ in range(args.steps):
-        step()
+        timed()
     e1.record()
     torch.cuda.synchronize()
     w1t = time.time()
     barrier()
-    launches = lib.tfb200_launch_count() - l0
+    launches = lib.tfb200_launch_count() - l0 + launches_per_replay * args.steps
     ms = e0.elapsed_time(e1)
+    ms_by_rank = [ms]
     if world > 1:
-        tt = torch.tensor([ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
+        allms = [torch.zeros(1, dtype=torch.float64, device="cuda") for _ in range(world)]
+        dist.all_gather(allms, torch.tensor([ms], dtype=torch.float64, device="cuda"))
+        ms_by_rank = [float(t.item()) for t in allms]
+        ms = max(ms_by_rank)
     clocks = sampler.stop(w0, w1t) if sampler else None
     ms_step = ms / args.steps
     if tp:
@@ -554,6 +577,8 @@ def run_ours(args) -> int:
                         "step, on copy streams overlapping the neighbouring steps' compute (double-buffered); "
                         "weights resident"},
         "gpu_launches": launches,
+        "launch": "CUDA graph of one step, replayed" if graph is not None else "eager public call per step",
+        "ms_per_step_by_rank": [round(v / args.steps, 5) for v in ms_by_rank],
         "clocks": clocks,
     }
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
@@ -570,6 +595,7 @@ def run_ours(args) -> int:
                                           f"restated (numpy/OpenBLAS fp32, libm erf per element)"}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    del graph
     if fused_tp:
         barrier()
         mlp.close()
@@ -593,6 +619,8 @@ def main() -> int:
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                     help="prefill workloads under torchrun: split the workload's rows over the ranks (strong) or "
                          "give every rank all of them (weak)")
+    ap.add_argument("--eager", action="store_true",
+                    help="time the public call per step instead of a CUDA-graph replay of one step")
     ap.add_argument("--shard-of", type=int, default=0,
                     help="time rank 0's share of an N-way row split on this one GPU (prefill workloads)")
     args = ap.parse_args()
