@@ -11,8 +11,8 @@ is fixed, `value` is the whole job's TFLOP/s); `--scaling weak` gives every
 rank its own 8192 rows instead. `--shard-of N` times, on one GPU, the share
 one rank has in an N-way split. Timing: W untimed warm-up steps,
 then exactly K steps between barrier + synchronize pairs, CUDA events on the
-launching stream, max over ranks; the timed steps replay one step recorded in
-a CUDA graph (`--eager`: the public call per step). `e2e` always runs the
+launching stream, max over ranks; the K timed steps are recorded in a CUDA
+graph and replayed (`--eager`: the public call per step). `e2e` always runs the
 public call with host buffers. Inputs (W1 + W2 + X = 320 MiB) exceed the
 126 MB L2, so no flush is needed between steps.
 
@@ -453,23 +453,21 @@ def run_ours(args) -> int:
         step()
     barrier()
     torch.cuda.synchronize()
-    # The timed loop replays one step recorded in a CUDA graph, as a serving loop runs a fixed-shape step: the
-    # same kernels and arguments as the eager call, without the host's per-call work (argument checks, tensor
-    # maps, three launches: about 54 us per call, which eight ranks sharing the host's cores do not all hide
-    # behind a 200 us step). `--eager` times the public call itself. The path with an NCCL all-reduce stays
-    # eager.
+    # The K timed steps are recorded once in a CUDA graph and replayed, as a serving loop runs fixed-shape steps:
+    # the same kernels and arguments as K eager calls (the programmatic-launch chaining between consecutive steps
+    # included), without the host's per-call work (argument checks, tensor maps, launches: about 54 us per call,
+    # which eight ranks sharing the host's cores do not all hide behind a 200 us step). `--eager` times the
+    # public call itself. The path with an NCCL all-reduce stays eager.
     graph = None
-    timed = step
-    launches_per_replay = 0
+    launches_in_graph = 0
     if not args.eager and not (tp and world > 1 and not fused_tp):
         graph = torch.cuda.CUDAGraph()
         lc = lib.tfb200_launch_count()
         with torch.cuda.graph(graph):
-            step()
-        launches_per_replay = lib.tfb200_launch_count() - lc
-        timed = graph.replay
-        for _ in range(2):
-            timed()
+            for _ in range(args.steps):
+                step()
+        launches_in_graph = lib.tfb200_launch_count() - lc
+        graph.replay()  # untimed: the graph's first replay uploads it
         torch.cuda.synchronize()
         barrier()
     e0 = torch.cuda.Event(enable_timing=True)
@@ -477,13 +475,16 @@ def run_ours(args) -> int:
     l0 = lib.tfb200_launch_count()
     w0 = time.time()
     e0.record()
-    for _ in range(args.steps):
-        timed()
+    if graph is not None:
+        graph.replay()
+    else:
+        for _ in range(args.steps):
+            step()
     e1.record()
     torch.cuda.synchronize()
     w1t = time.time()
     barrier()
-    launches = lib.tfb200_launch_count() - l0 + launches_per_replay * args.steps
+    launches = lib.tfb200_launch_count() - l0 + launches_in_graph
     ms = e0.elapsed_time(e1)
     ms_by_rank = [ms]
     if world > 1:
@@ -577,7 +578,8 @@ def run_ours(args) -> int:
                         "step, on copy streams overlapping the neighbouring steps' compute (double-buffered); "
                         "weights resident"},
         "gpu_launches": launches,
-        "launch": "CUDA graph of one step, replayed" if graph is not None else "eager public call per step",
+        "launch": f"CUDA graph of the {args.steps} timed steps, replayed once" if graph is not None
+        else "eager public call per step",
         "ms_per_step_by_rank": [round(v / args.steps, 5) for v in ms_by_rank],
         "clocks": clocks,
     }

@@ -33,11 +33,15 @@ static int check(int T, int KB, int P, int max_slots, int gain, int per_helper) 
   std::vector<int> slot_writes(kMaxSlots * kMaxParts + 1, 0);
   std::map<int, int> main_first_slot;  // tile -> first slot
   int64_t busiest_seen = 0;
+  std::map<int, int> tile_main;  // split tile -> its main pair
+  std::vector<std::pair<int, int>> part_writers;  // (tile, helper pair)
   for (int p = 0; p < P; ++p) {
     const int n = work_count(s, p);
     int64_t load = 0;
     for (int i = 0; i < n; ++i) {
       const Work w = work_item(s, p, i);
+      if (w.role == kMain) tile_main[w.tile] = p;
+      if (w.role == kPart) part_writers.push_back({w.tile, p});
       if (w.tile < 0 || w.tile >= T || w.k0 < 0 || w.k1 > KB || w.k0 >= w.k1) return fail("item range", T, KB, P);
       for (int k = w.k0; k < w.k1; ++k) ++cover[static_cast<size_t>(w.tile) * KB + k];
       load += w.k1 - w.k0;
@@ -58,6 +62,9 @@ static int check(int T, int KB, int P, int max_slots, int gain, int per_helper) 
   }
   for (int v : cover)
     if (v != 1) return fail("coverage", T, KB, P);
+  // a main pair waits only on pairs with lower indices
+  for (auto& tw : part_writers)
+    if (tw.second >= tile_main[tw.first]) return fail("helper index not below its main", T, KB, P);
   for (int g = 0; g < s.rem * s.parts; ++g)
     if (slot_writes[g] != 1) return fail("slot written once", T, KB, P);
   for (int r = 0; r < s.rem; ++r) {

@@ -52,9 +52,11 @@ def test_version_and_workspace(L):
     base = 8192 * 16384 * 2 + 8192 * 4096 * 2 + 8192 * 4
     assert lib.tfb200_fused_mlp_workspace_size(8192, 4096, 16384, 4096) == base + 2 * flags + 128 * slot
     assert lib.tfb200_fused_mlp_workspace_size(0, 4096, 16384, 4096) == 0
-    # few rows: the streamed path adds fp32 accumulators and column-block counters
-    assert lib.tfb200_fused_mlp_workspace_size(3, 8, 5, 8) == 7 * 256
-    assert lib.tfb200_fused_mlp_partial_workspace_size(3, 8, 5, 8) == 6 * 256
+    # few rows: the streamed path adds the streaming kernel's partial-sum slots (one fp32 [m, 128] per column block
+    # plus one per CTA beyond the first, up to 160 CTAs) and the column-block counters with the phase barrier
+    streamed = 256 + 512 + (1 + 160 - 1) * 3 * 128 * 4 + 256
+    assert lib.tfb200_fused_mlp_workspace_size(3, 8, 5, 8) == streamed
+    assert lib.tfb200_fused_mlp_partial_workspace_size(3, 8, 5, 8) == streamed
     # 128 rows run on the one-CTA kernel: no split region
     assert lib.tfb200_fused_mlp_workspace_size(128, 128, 128, 128) == 128 * 128 * 2 + 128 * 128 * 2 + 512
     assert lib.tfb200_fused_rmsnorm_matmul_workspace_size(8192, 4096, 6144) == (8192 * 4096 * 2 + 8192 * 4 + flags

@@ -52,19 +52,22 @@ struct GemmProblem {
 // a message in *err.
 int run_gemm(const GemmProblem& p, cudaStream_t stream, std::string* err);
 
-// Weight-streaming GEMM for few rows (stream_sm100.cu): acc[M,N] (+)= A[M,K] @ W[K,N]
-// split over all SMs, then a per-column-block finishing epilogue.
+// Weight-streaming fused MLP for few rows (stream_sm100.cu): one persistent
+// launch runs one or two phases, each acc[M,N] = A[M,K] @ W[K,N] split over all
+// SMs (partial sums in per-CTA slots, added in CTA order by the CTA that
+// completes a 128-column block), then a per-column-block finishing epilogue;
+// a grid barrier separates the phases (phase 1 reads what phase 0 wrote).
 enum StreamMode : int { kStreamPartial = 0, kStreamFinishUp = 1, kStreamFinishDown = 2, kStreamTpReduce = 3 };
 constexpr int kMaxTp = 8;
 // Tensor-parallel reduction fused into the down-projection (kStreamTpReduce).
-// Each rank first sums its CTAs' partials for a 128-column block in its own
-// accumulator (L2 atomics). On a rank that does not own the block (owner =
-// nb % world), the CTA that completes it locally pushes it, M x 128 fp32 in
-// 16-byte stores, into its slot on the owner and arrives on the owner's
-// counter. On the owner, that CTA waits for the other ranks' arrivals, adds
-// the slots and its own sums in rank order plus the residual, rounds, writes
-// the block to every rank's output and bumps every rank's done counter.
-// Counters and accumulators are returned to zero by the CTAs done with them.
+// Each rank first sums its CTAs' partials for a 128-column block (slots added
+// in CTA order) into its local buffer. On a rank that does not own the block
+// (owner = nb % world), the CTA that completes it locally pushes it, M x 128
+// fp32 in 16-byte stores, into its slot on the owner and arrives on the
+// owner's counter. On the owner, that CTA waits for the other ranks' arrivals,
+// adds the slots and its own sums in rank order plus the residual, rounds,
+// writes the block to every rank's output and bumps every rank's done counter.
+// Counters are returned to zero by the CTAs done with them.
 struct TpPeers {
   int rank = 0, world = 1;
   int64_t slot_stride = 0;          // elements between two source slots (rows capacity x N)
@@ -80,27 +83,36 @@ struct TpLayout {
   size_t acc, local_cnt, slots, arrive, out, done, total;
 };
 TpLayout tp_layout(int64_t max_rows, int64_t n, int world);
-struct StreamProblem {
-  int64_t M = 0, N = 0, K = 0;
-  const bf16* A = nullptr;  // [M, K] tokens
+struct StreamPhase {
+  int64_t N = 0, K = 0;
+  const bf16* A = nullptr;  // [M, K] tokens (phase 1: the block phase 0 writes)
   int64_t lda = 0;
   const bf16* W = nullptr;  // [K, N] weights
   int64_t ldw = 0;
-  float* acc = nullptr;     // [M, N] fp32, zero on entry
-  int* counters = nullptr;  // ceil(N / 128) ints, zero on entry
   int mode = kStreamPartial;
+  int* counters = nullptr;           // ceil(N / 128) ints, zero on entry
   const float* col_scale = nullptr;  // [M] (kStreamFinishUp)
   const bf16* bias = nullptr;        // [N] (kStreamFinishUp)
   int gelu = kGeluNone;
-  const bf16* residual = nullptr;    // [M, N] (kStreamFinishDown)
+  const bf16* residual = nullptr;    // [M, N] (kStreamFinishDown, kStreamTpReduce)
   int64_t ldr = 0;
-  bf16* out = nullptr;
+  bf16* out = nullptr;               // kStreamFinishUp / kStreamFinishDown
   int64_t ldo = 0;
-  TpPeers tp;  // kStreamTpReduce
+  float* part = nullptr;             // kStreamPartial: fp32 result; kStreamTpReduce: this rank's sums [M, N]
+  int64_t ldp = 0;
+};
+struct StreamProblem {
+  int64_t M = 0;
+  StreamPhase ph[2];
+  int nphases = 1;
+  float* slots = nullptr;   // stream_slot_bytes(M, largest N of the phases)
+  int* grid_bar = nullptr;  // one int, zero on entry (two phases)
+  TpPeers tp;               // kStreamTpReduce
 };
 int run_stream(const StreamProblem& p, cudaStream_t stream, std::string* err);
 int stream_mpad(int64_t m);
 size_t stream_counter_bytes(int64_t n);
+size_t stream_slot_bytes(int64_t m, int64_t n_max);
 
 // Streamed (decode-shaped) fused MLP, decode.cu. Used for M <= kStreamMaxRows.
 constexpr int64_t kStreamMaxRows = cfg::kStreamMaxRows;

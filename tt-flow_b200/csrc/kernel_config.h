@@ -28,6 +28,8 @@ constexpr int kGroupM = 16;  // raster group of both tiled kernels (row tiles)
 constexpr int kStreamMaxRows = 64;
 constexpr int kStreamN = 128, kStreamK = 64, kStreamMaxStages = 12, kStreamBudget = 200 * 1024;
 constexpr int kStreamAcc = 4;
+// Most CTAs of the weight-streaming kernel (one per SM; sizes its partial-sum slots).
+constexpr int kStreamMaxGrid = 160;
 constexpr int kStreamCtlBytes = 280;
 
 }  // namespace tfb200::cfg

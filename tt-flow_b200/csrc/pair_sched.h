@@ -8,14 +8,19 @@
 // P the last wave holds only R = T % P tiles, and P - R pairs would idle while
 // it runs (at 1024 rows per GPU: 64 down-projection tiles on 74 pairs, 13.5 %
 // of the step). The tail split fills that wave:
-//   * main pair r (r < R) computes k-blocks [0, kc) of remainder tile r and
-//     finishes the tile;
+//   * main pair H + r (r < R, H = P - R) computes k-blocks [0, kc) of
+//     remainder tile r and finishes the tile;
 //   * the remaining k-blocks [kc, KB) of every remainder tile are cut into S
-//     equal parts, and the P - R helper pairs take the R * S parts in contiguous
-//     runs. A helper writes each part's fp32 accumulator to its own slot in the
+//     equal parts, and the helper pairs 0 .. H-1 take the R * S parts in
+//     contiguous runs. A helper writes each part's fp32 accumulator to its own slot in the
 //     caller's workspace and raises a flag; the main pair waits for the S flags
 //     of its tile, adds the slots in part order to its own accumulator (a fixed
 //     order: the result does not depend on timing) and runs the epilogue.
+// A main pair waits only on pairs with lower indices. The hardware dispatches
+// a grid's CTAs in index order, so when a main is resident its helpers have
+// been dispatched and finish without waiting on anything; this holds however
+// many other kernels share the SMs (the rule that decoupled look-back scans
+// rely on).
 // All main pairs stream the same k rows of the shared weight panels at the same
 // time, as the full waves do, so the weights still cross HBM about once; only
 // the short tails [kc, KB) are re-read by the helpers, from L2. (A plain
@@ -62,7 +67,7 @@ TFB_SCHED_HD int part_lo(const PairSched& s, int j) {
   return s.kc + static_cast<int>(static_cast<int64_t>(s.kblocks - s.kc) * j / s.parts);
 }
 
-// Helper h (0 <= h < P - R) takes parts [part_begin(h), part_begin(h + 1)).
+// Helper h (pair h, 0 <= h < P - R) takes parts [part_begin(h), part_begin(h + 1)).
 TFB_SCHED_HD int part_begin(const PairSched& s, int h) {
   const int helpers = s.pairs - s.rem;
   return static_cast<int>(static_cast<int64_t>(s.rem) * s.parts * h / helpers);
@@ -139,9 +144,9 @@ struct Work {
 // Number of work items of pair p.
 TFB_SCHED_HD int work_count(const PairSched& s, int p) {
   if (s.rem == 0) return p < s.tiles ? static_cast<int>((s.tiles - 1 - p) / s.pairs + 1) : 0;
-  if (p < s.rem) return s.waves + 1;
-  const int h = p - s.rem;
-  return s.waves + part_begin(s, h + 1) - part_begin(s, h);
+  const int helpers = s.pairs - s.rem;
+  if (p >= helpers) return s.waves + 1;
+  return s.waves + part_begin(s, p + 1) - part_begin(s, p);
 }
 
 // Work item i (0 <= i < work_count(s, p)) of pair p, in the order the pair
@@ -157,15 +162,17 @@ TFB_SCHED_HD Work work_item(const PairSched& s, int p, int i) {
     return w;
   }
   const int base = s.waves * s.pairs;
-  if (p < s.rem) {
-    w.tile = base + p;
+  const int helpers = s.pairs - s.rem;
+  if (p >= helpers) {
+    const int r = p - helpers;
+    w.tile = base + r;
     w.k0 = 0;
     w.k1 = s.kc;
     w.role = kMain;
-    w.slot = p * s.parts;
+    w.slot = r * s.parts;
     return w;
   }
-  const int g = part_begin(s, p - s.rem) + (i - s.waves);
+  const int g = part_begin(s, p) + (i - s.waves);
   const int r = g / s.parts, j = g - r * s.parts;
   w.tile = base + r;
   w.k0 = part_lo(s, j);
