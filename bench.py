@@ -44,11 +44,13 @@ METRIC = "fused RMSNorm+MatMul / MLP TFLOP/s & % bf16 tensor peak at 1/2/4/8 B20
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes moved by the dominant kernel per launch (dram__bytes_read.sum +
 # dram__bytes_write.sum, averaged over the kernel's launches in one step), from the
-# ncu captures summarised in profiles/k_gemm_mlp_8192x4096x16384.md and
+# ncu captures summarised in profiles/k_gemm_mlp_8192x4096x16384.md,
+# profiles/k_gemm_pair_qkv_8192x4096x6144.md and
 # profiles/k_stream_decode_mlp_32x8192x28672.md.
 TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {
-    "mlp_8192x4096x16384": (439.884e6 + 253.001e6 + 1326.001e6 + 62.057e6) / 2,
-    "decode_mlp_32x8192x28672": (476.727e6 + 8.738e6 + 474.788e6 + 4.495e6) / 2,
+    "mlp_8192x4096x16384": (433.472e6 + 252.322e6 + 1319.072e6 + 61.671e6) / 2,
+    "qkv_8192x4096x6144": 209.118e6 + 86.456e6,
+    "decode_mlp_32x8192x28672": (470.603e6 + 4.898e6 + 472.422e6 + 3.828e6) / 2,
 }
 
 

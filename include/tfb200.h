@@ -76,8 +76,11 @@ const char* tfb200_last_error(void);
  * K == 0 writes zeros; M == 0 or N == 0 is a no-op. */
 int tfb200_matmul(const tfb200_mat* a, const tfb200_mat* b, tfb200_mat* c, void* stream);
 
-/* Bytes of device workspace tfb200_fused_rmsnorm_matmul needs for M rows of
- * width K (the staged bf16(x * gamma) block and the per-row inverse RMS). */
+/* Bytes of device workspace tfb200_fused_rmsnorm_matmul takes for M rows of
+ * width K and N outputs: the staged bf16(x * gamma) block and the per-row
+ * inverse RMS, plus the fp32 slots and flags of the GEMM's tail split (a short
+ * last wave of tiles spread over idle CTA pairs). A workspace that holds only
+ * the first part is accepted and runs without the split. */
 size_t tfb200_fused_rmsnorm_matmul_workspace_size(int64_t m, int64_t k, int64_t n);
 
 /* Y = rmsnorm(X, gamma, eps) @ W with rmsnorm(x) = x / sqrt(mean_k(x^2) + eps) * gamma.
@@ -93,9 +96,12 @@ size_t tfb200_fused_rmsnorm_matmul_workspace_size(int64_t m, int64_t k, int64_t 
 int tfb200_fused_rmsnorm_matmul(const tfb200_mat* x, const void* gamma, const tfb200_mat* w, float eps,
                                 tfb200_mat* y, void* stream, void* workspace, size_t workspace_bytes);
 
-/* Bytes of device workspace tfb200_fused_mlp needs for M rows, K model width,
- * H hidden width and N output width (the bf16 hidden activation block plus the
- * RMSNorm staging of tfb200_fused_rmsnorm_matmul_workspace_size). */
+/* Bytes of device workspace tfb200_fused_mlp takes for M rows, K model width,
+ * H hidden width and N output width: the bf16 hidden activation block, the
+ * RMSNorm staging, and the tail-split slots of the two GEMMs (M > 64) or the
+ * partial-sum slots and counters of the weight-streaming kernel (M <= 64). For
+ * M > 64 a workspace without the tail-split slots is accepted and runs without
+ * the split. */
 size_t tfb200_fused_mlp_workspace_size(int64_t m, int64_t k, int64_t h, int64_t n);
 
 /* Y = gelu(rmsnorm(X, gamma, eps) @ W1 + b1) @ W2 + R.
