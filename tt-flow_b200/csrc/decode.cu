@@ -47,6 +47,21 @@ bool two_launches() {
   return two;
 }
 
+// Units (64 x 128 weight tiles, 16 KiB) per CTA of the down-projection's
+// weights prefetched into L2 while the up-projection drains: 32 x 16 KiB x 148
+// CTAs = 78 MB, inside the 126 MB L2. Measured on B200 at 32 x 8192 x 28672
+// (us per step, two runs each): none 171.9 / 172.6, 24 units 166.7 / 166.8,
+// 32 units 166.3 / 166.4, 48 units 167.5 / 167.7, 64 units 170.3 / 170.6 (the
+// prefetched tiles no longer fit beside the stream). TFB200_STREAM_PREFETCH
+// overrides it (0 turns it off).
+int prefetch_units() {
+  static const int n = [] {
+    const char* v = std::getenv("TFB200_STREAM_PREFETCH");
+    return v ? std::atoi(v) : 32;
+  }();
+  return n;
+}
+
 }  // namespace
 
 // Workspace of the streamed MLP: hidden block, staging, the partial-sum slots
@@ -143,6 +158,7 @@ int run_decode_mlp(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* w1
     dn.out = y;
     dn.ldo = ldy;
   }
+  sp.prefetch_units = prefetch_units();
   if (!two_launches()) return run_stream(sp, s, err);
   // The two phases as two launches (chained with programmatic dependent
   // launch): the down-projection's launch waits for the up-projection's grid.
@@ -150,6 +166,8 @@ int run_decode_mlp(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* w1
   a1.nphases = 1;
   a2.nphases = 1;
   a2.ph[0] = sp.ph[1];
+  a1.next = sp.ph[1];
+  a2.prefetch_units = 0;
   rc = run_stream(a1, s, err);
   if (rc) return rc;
   return run_stream(a2, s, err);

@@ -108,6 +108,14 @@ struct StreamProblem {
   float* slots = nullptr;   // stream_slot_bytes(M, largest N of the phases)
   int* grid_bar = nullptr;  // one int, zero on entry (two phases)
   TpPeers tp;               // kStreamTpReduce
+  // Optional, one phase: the weights of the streaming launch that follows on
+  // the same stream (only next.W, ldw, N, K are read). Once a CTA has issued its
+  // own weight stream it prefetches into L2 the first prefetch_units units of
+  // the range the same CTA of that launch will stream, so HBM stays busy while
+  // this launch drains. With two phases, prefetch_units units of phase 1 past
+  // the shared-memory ring are prefetched before the phase barrier.
+  StreamPhase next;
+  int prefetch_units = 0;
 };
 int run_stream(const StreamProblem& p, cudaStream_t stream, std::string* err);
 int stream_mpad(int64_t m);

@@ -31,5 +31,7 @@ constexpr int kStreamAcc = 4;
 // Most CTAs of the weight-streaming kernel (one per SM; sizes its partial-sum slots).
 constexpr int kStreamMaxGrid = 160;
 constexpr int kStreamCtlBytes = 280;
+// Row scales (1/rms) the up-projection's finishers read, staged after the control block.
+constexpr int kStreamScaleBytes = kStreamMaxRows * 4;
 
 }  // namespace tfb200::cfg

@@ -163,6 +163,14 @@ __device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap
       : "memory");
 }
 
+// 2-D tile of a tensor map brought into L2 (no shared memory, no completion
+// signal). Coordinates outside the tensor are skipped by the copy engine.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* m, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(m)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 // 2-D tiled load issued by either CTA of a CTA pair; completion is signalled
 // on the barrier at `bar_cluster` (a shared::cluster address, here the leader
 // CTA's barrier). Each CTA loads only its own tile.

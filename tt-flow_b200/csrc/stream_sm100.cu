@@ -33,7 +33,10 @@
 // whole. The phase-1 weight tiles that fit the shared-memory ring are
 // requested before the barrier; the hidden block follows once every CTA has
 // arrived. Launched with programmatic stream serialization: the prologue and
-// the first ring of weight tiles overlap the preceding grid's tail.
+// the first ring of weight tiles overlap the preceding grid's tail. A CTA that
+// has issued its whole weight stream also prefetches into L2 the first units of
+// the range it (or the same CTA of the next launch) streams next, so that HBM
+// keeps streaming while the slowest CTAs and the finishers drain.
 //
 // Warp roles: warp 0 TMA producer (W tile 64k x 128n as two 64-column boxes,
 // A tile Mpad x 64k), warp 1 MMA issuer (tcgen05.mma 128 x Mpad x 16, kAcc TMEM
@@ -87,6 +90,9 @@ struct SParams {
   int* status;
   uint64_t timeout_ns;
   TpPeers tp;
+  // L2 prefetch of the weights streamed next (tmW1): pf_units units of the
+  // range this CTA streams there, after skipping pf_skip of them.
+  int pf_units, pf_skip, pf_kblocks, pf_total;
 };
 
 // TMEM accumulators in rotation: the MMA may run kAcc-1 segments ahead of the
@@ -452,6 +458,22 @@ __device__ __forceinline__ bool produce(const SParams& p, SCtl* ctl, const CUten
   return true;
 }
 
+// Units [u0 + skip, u0 + skip + pf_units) of the range [u0, u1) this CTA
+// streams from tmW next (the next launch's weights, or phase 1), brought into
+// L2 with the same unit -> (column block, k block) order as produce().
+__device__ __forceinline__ void prefetch_next_weights(const SParams& p, const CUtensorMap* tmW) {
+  const int64_t u0 = unit_start(blockIdx.x, p.pf_total, gridDim.x);
+  const int64_t u1 = unit_start(blockIdx.x + 1, p.pf_total, gridDim.x);
+  int64_t e = u0 + p.pf_skip + p.pf_units;
+  if (e > u1) e = u1;
+  for (int64_t u = u0 + p.pf_skip; u < e; ++u) {
+    const int nb = static_cast<int>(u / p.pf_kblocks);
+    const int kb = static_cast<int>(u - static_cast<int64_t>(nb) * p.pf_kblocks);
+    tma_prefetch_l2_2d(tmW, nb * SBN, kb * SBK);
+    tma_prefetch_l2_2d(tmW, nb * SBN + 64, kb * SBK);
+  }
+}
+
 // -------------------------------------------------------------- MMA issuer
 
 template <int PH>
@@ -537,6 +559,13 @@ __device__ __forceinline__ bool epilogue_phase(const SParams& p, SCtl* ctl, uint
   const int q = warp & 3;
   const int et = threadIdx.x - 128;  // 0..127
   const int64_t slot_elems = static_cast<int64_t>(p.M) * SBN;
+  // The finishers' row scales (1/rms), staged once per phase in shared memory:
+  // read from global memory at finishing time they cost an L2 round trip.
+  float* s_scale = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ctl) + sizeof(SCtl));
+  if (f.mode == kStreamFinishUp) {
+    if (et < p.M) s_scale[et] = __ldg(f.col_scale + et);
+    epi_bar();
+  }
   for (int si = 0; si < segs.n; ++si, ++gseg) {
     int64_t s0, e0;
     int nb;
@@ -604,25 +633,32 @@ __device__ __forceinline__ bool epilogue_phase(const SParams& p, SCtl* ctl, uint
       tp_push_and_finish(p, f, ctl, nb, et, res);
       continue;
     }
-    // Unrolled over the row batches: the residual registers are then indexed
-    // with constants.
+    // Every row batch's slot loads are issued before the first store: a store
+    // may alias the slots, so loads placed after one wait for it, and a
+    // load-store chain per batch cost about 3 us of the up-projection's finish
+    // (measured with per-CTA timestamps on B200 at 32 x 8192 x 28672: step
+    // 166 -> 159 us together with the staged row scales). The batch loop is
+    // unrolled, so the residual registers are indexed with constants.
+    constexpr int kBatches = static_cast<int>(kStreamMaxRows / kSumRows);
+    float vals[kBatches][kSumRows];
+#pragma unroll
+    for (int b = 0; b < kBatches; ++b)
+      if (b * kSumRows < p.M) sum_slots(p, nb, c_first, c_last, et, b * kSumRows, vals[b]);
 #pragma unroll
     for (int m0 = 0; m0 < kStreamMaxRows; m0 += kSumRows) {
       if (m0 >= p.M) break;
-      float val[kSumRows];
-      sum_slots(p, nb, c_first, c_last, et, m0, val);
       if (!col_ok) continue;
 #pragma unroll
       for (int j = 0; j < kSumRows; ++j) {
         const int m = m0 + j;
         if (m >= p.M) break;
-        float v = val[j];
+        float v = vals[m0 / kSumRows][j];
         if (f.mode == kStreamPartial) {
           f.part[static_cast<int64_t>(m) * f.ldp + nf] = v;
           continue;
         }
         if (f.mode == kStreamFinishUp) {
-          v = v * __ldg(f.col_scale + m) + bias;
+          v = v * s_scale[m] + bias;
           v = f.gelu == kGeluErf ? gelu_erf(v) : (f.gelu == kGeluTanh ? gelu_tanh(v) : v);
         } else {
           v += residual_at(res, m);
@@ -665,6 +701,8 @@ __global__ void __launch_bounds__(256, 1)
     if (p.nph > 1) {
       tma_prefetch_desc(&tmW1);
       tma_prefetch_desc(&tmA1);
+    } else if (p.pf_units > 0) {
+      tma_prefetch_desc(&tmW1);
     }
   }
   if (warp == 2) {
@@ -689,6 +727,7 @@ __global__ void __launch_bounds__(256, 1)
       // barrier.
       Ring ring{};
       bool ok = produce<0>(p, ctl, &tmW0, &tmA0, sW, sA, a_stage, ring);
+      if (ok && p.pf_units > 0) prefetch_next_weights(p, &tmW1);
       if (ok && p.nph > 1) ok = produce<1>(p, ctl, &tmW1, &tmA1, sW, sA, a_stage, ring);
       if (!ok) {
         for (int s = 0; s < p.stages; ++s)
@@ -827,7 +866,8 @@ int run_stream(const StreamProblem& sp, cudaStream_t stream, std::string* err) {
   uint32_t cols = 32;
   while (cols < static_cast<uint32_t>(kAcc * p.Mpad)) cols <<= 1;
   p.tmem_cols = cols;
-  const size_t smem = 1024 + static_cast<size_t>(p.stages) * (W_STAGE + a_stage) + sizeof(SCtl);
+  const size_t smem =
+      1024 + static_cast<size_t>(p.stages) * (W_STAGE + a_stage) + sizeof(SCtl) + cfg::kStreamScaleBytes;
 
   CUtensorMap tw0{}, ta0{}, tw1{}, ta1{};
   const StreamPhase& f0 = sp.ph[0];
@@ -837,6 +877,9 @@ int run_stream(const StreamProblem& sp, cudaStream_t stream, std::string* err) {
     const StreamPhase& f1 = sp.ph[1];
     if (!make_map(&tw1, f1.W, f1.K, f1.N, f1.ldw, SBK, err)) return -3;
     if (!make_map(&ta1, f1.A, sp.M, f1.K, f1.lda, static_cast<uint32_t>(p.Mpad), err)) return -3;
+  } else if (sp.prefetch_units > 0 && sp.next.W) {
+    if (!make_map(&tw1, sp.next.W, sp.next.K, sp.next.N, sp.next.ldw, SBK, err)) return -3;
+    ta1 = ta0;
   } else {
     tw1 = tw0;
     ta1 = ta0;
@@ -862,6 +905,26 @@ int run_stream(const StreamProblem& sp, cudaStream_t stream, std::string* err) {
   int grid = sm_count() < cfg::kStreamMaxGrid ? sm_count() : cfg::kStreamMaxGrid;
   for (int i = 0; i < p.nph; ++i)
     if (p.ph[i].units < grid) grid = p.ph[i].units;
+  // L2 prefetch of the weights streamed next. For the next launch this holds
+  // only when that launch gets the same grid (the same CTA -> range map).
+  if (sp.prefetch_units > 0) {
+    if (p.nph > 1) {
+      p.pf_units = sp.prefetch_units;
+      p.pf_skip = p.stages;  // phase 1's first ring is loaded before the phase barrier
+      p.pf_kblocks = p.ph[1].kblocks;
+      p.pf_total = p.ph[1].units;
+    } else if (sp.next.W) {
+      const SPhase nx = make_phase(sp.next);
+      int grid_next = sm_count() < cfg::kStreamMaxGrid ? sm_count() : cfg::kStreamMaxGrid;
+      if (nx.units < grid_next) grid_next = nx.units;
+      if (grid_next == grid) {
+        p.pf_units = sp.prefetch_units;
+        p.pf_skip = 0;
+        p.pf_kblocks = nx.kblocks;
+        p.pf_total = nx.units;
+      }
+    }
+  }
   // Programmatic dependent launch: this grid's prologue and first ring of
   // weight tiles overlap the tail of the preceding grid (TFB200_PDL=0 turns it off).
   static const bool pdl = [] {

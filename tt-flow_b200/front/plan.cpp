@@ -87,7 +87,7 @@ B200Plan plan_b200(const PlanRequest& r) {
     p.tile_n = mpad;
     p.tile_k = kStreamK;
     p.stages = std::min<int64_t>(kStreamMaxStages, kStreamBudget / (w_stage + a_stage));
-    p.smem_bytes = 1024 + p.stages * (w_stage + a_stage) + kStreamCtlBytes;
+    p.smem_bytes = 1024 + p.stages * (w_stage + a_stage) + kStreamCtlBytes + cfg::kStreamScaleBytes;
     int64_t cols = 32;
     while (cols < kStreamAcc * mpad) cols <<= 1;
     p.tmem_columns = cols;
