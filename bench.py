@@ -50,7 +50,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {
     "mlp_8192x4096x16384": (433.472e6 + 252.322e6 + 1319.072e6 + 61.671e6) / 2,
     "qkv_8192x4096x6144": 209.118e6 + 86.456e6,
-    "decode_mlp_32x8192x28672": (470.603e6 + 4.898e6 + 472.422e6 + 3.828e6) / 2,
+    "decode_mlp_32x8192x28672": (524.275e6 + 4.995e6 + 472.344e6 + 3.566e6) / 2,
 }
 
 
