@@ -911,6 +911,17 @@ int split_min_gain_permille() {
   return v;
 }
 
+// Most tail parts one helper pair takes (pair_sched.h plan()); 1 unless
+// TFB200_GEMM_PARTS_PER_HELPER says otherwise (for measurements).
+int parts_per_helper() {
+  static const int v = [] {
+    const char* e = std::getenv("TFB200_GEMM_PARTS_PER_HELPER");
+    const int n = e ? std::atoi(e) : 1;
+    return n >= 1 ? n : 1;
+  }();
+  return v;
+}
+
 template <bool MANUAL>
 int launch(const KParams& kp, const CUtensorMap& ta, const CUtensorMap& tb, int grid, cudaStream_t s,
            std::string* err) {
@@ -994,7 +1005,8 @@ int launch_pair_g(const KParams& kp_in, const CUtensorMap& ta, const CUtensorMap
   KParams kp = kp_in;
   const int kblocks = (kp.K + BK - 1) / BK;
   const int gain = split_min_gain_permille();
-  kp.ps = sched::plan(pair_tiles, kblocks, max_clusters[dev], gain >= 0 ? max_slots : 0, gain >= 0 ? gain : 0);
+  kp.ps = sched::plan(pair_tiles, kblocks, max_clusters[dev], gain >= 0 ? max_slots : 0, gain >= 0 ? gain : 0,
+                      parts_per_helper());
   if (kp.ps.rem == 0) {
     const int used = pair_tiles < max_clusters[dev] ? pair_tiles : max_clusters[dev];
     kp.ps = sched::plan(pair_tiles, kblocks, used, 0);

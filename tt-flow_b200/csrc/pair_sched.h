@@ -91,7 +91,11 @@ TFB_SCHED_HD int64_t busiest(const PairSched& s) {
 // and gives no helper more than max_per_helper parts. (Measured on B200 at
 // 1024 x 16384 x 4096: helpers that ran 6-7 parts each streamed about 30 %
 // slower than the main pairs, and the split launch took 116 us against 107 us
-// without it; with one part per helper the splits of the other shapes gained.)
+// without it; with one part per helper the splits of the other shapes gained.
+// For the 1024-row down-projection, 64 tiles on 74 pairs, seven parts per
+// helper would cut the busiest pair from 256 to 224 k-blocks, but the MLP step
+// measured 212.5-212.9 us against 206.8-207.2 us without the split; at 2048
+// rows four parts per helper gained 1.3-2.7 % (378-383 us against 388 us).)
 TFB_SCHED_HD PairSched plan(int T, int KB, int P, int max_slots, int min_gain_permille = 20,
                             int max_per_helper = 1) {
   PairSched dp;
