@@ -146,6 +146,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_rms_prep_reg(const bf16* __rest
 // and CTAs past the last row clear `zero` (the streamed GEMMs' fp32
 // accumulators and counters) with 16-byte stores.
 constexpr int kRowThreads = 256;
+constexpr int kRowChunks = 4;  // 16-byte chunks per thread held in registers: rows of up to 8192 elements
 
 __global__ void __launch_bounds__(kRowThreads) k_rms_prep_rows(const bf16* __restrict__ x, int64_t ldx,
                                                                const bf16* __restrict__ gamma, int M, int K,
@@ -163,15 +164,45 @@ __global__ void __launch_bounds__(kRowThreads) k_rms_prep_rows(const bf16* __res
   }
   const int64_t row = blockIdx.x;
   const uint4* xv = reinterpret_cast<const uint4*>(x + row * ldx);
+  const uint4* gv = reinterpret_cast<const uint4*>(gamma);
+  uint4* av = reinterpret_cast<uint4*>(a + row * lda);
   const int nchunk = K / 8;
   uint64_t ss2 = 0;
+  const bool in_regs = nchunk <= kRowChunks * kRowThreads;
+  if (in_regs) {
+    // The row and gamma in registers, all loads in flight together; bf16(x *
+    // gamma) does not depend on the sum, so it is written at once (one memory
+    // round trip on the decode step's critical path instead of two).
+    uint4 xr[kRowChunks], gr[kRowChunks];
+#pragma unroll
+    for (int i = 0; i < kRowChunks; ++i) {
+      const int c = threadIdx.x + i * kRowThreads;
+      if (c < nchunk) {
+        xr[i] = __ldg(xv + c);
+        gr[i] = __ldg(gv + c);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kRowChunks; ++i) {
+      const int c = threadIdx.x + i * kRowThreads;
+      if (c < nchunk) {
+        const uint4 v = xr[i], g = gr[i];
+        av[c] = make_uint4(mul_bf16x2(v.x, g.x), mul_bf16x2(v.y, g.y), mul_bf16x2(v.z, g.z), mul_bf16x2(v.w, g.w));
+        ss2 = sq_acc_bf16x2(ss2, v.x);
+        ss2 = sq_acc_bf16x2(ss2, v.y);
+        ss2 = sq_acc_bf16x2(ss2, v.z);
+        ss2 = sq_acc_bf16x2(ss2, v.w);
+      }
+    }
+  } else {
 #pragma unroll 4
-  for (int c = threadIdx.x; c < nchunk; c += kRowThreads) {
-    const uint4 v = __ldg(xv + c);
-    ss2 = sq_acc_bf16x2(ss2, v.x);
-    ss2 = sq_acc_bf16x2(ss2, v.y);
-    ss2 = sq_acc_bf16x2(ss2, v.z);
-    ss2 = sq_acc_bf16x2(ss2, v.w);
+    for (int c = threadIdx.x; c < nchunk; c += kRowThreads) {
+      const uint4 v = __ldg(xv + c);
+      ss2 = sq_acc_bf16x2(ss2, v.x);
+      ss2 = sq_acc_bf16x2(ss2, v.y);
+      ss2 = sq_acc_bf16x2(ss2, v.z);
+      ss2 = sq_acc_bf16x2(ss2, v.w);
+    }
   }
   float ss = __uint_as_float(static_cast<uint32_t>(ss2)) + __uint_as_float(static_cast<uint32_t>(ss2 >> 32));
 #pragma unroll
@@ -186,8 +217,7 @@ __global__ void __launch_bounds__(kRowThreads) k_rms_prep_rows(const bf16* __res
     s_inv = 1.0f / sqrtf(t / static_cast<float>(K) + eps);
     inv[row] = s_inv;
   }
-  const uint4* gv = reinterpret_cast<const uint4*>(gamma);
-  uint4* av = reinterpret_cast<uint4*>(a + row * lda);
+  if (in_regs) return;
 #pragma unroll 4
   for (int c = threadIdx.x; c < nchunk; c += kRowThreads) {
     const uint4 v = __ldg(xv + c);
