@@ -83,9 +83,12 @@ def test_mlp_block_small(ops, golden_vectors, gelu):
 
 # Above 1024 rows the staging pass holds each row in registers for K <= 4096
 # (K = 1000: lanes with 3 and 4 of the row's 125 16-byte chunks; K = 4096: 16 each)
-# and streams it twice above that (K = 4104).
+# and streams it twice above that (K = 4104). Up to 1024 rows (one CTA per row)
+# a row of up to 8192 elements is held in registers (K = 8192: four chunks per
+# thread) and longer rows are streamed twice (K = 8200, 16384).
 RAGGED = [(1, 64, 8), (200, 136, 300), (129, 64, 257), (300, 520, 40), (64, 4096, 1000), (70, 60, 33), (5, 7, 3),
-          (1100, 1000, 264), (2048, 4096, 256), (1030, 4104, 128)]
+          (1100, 1000, 264), (2048, 4096, 256), (1030, 4104, 128), (16, 8192, 136), (16, 8200, 136),
+          (3, 16384, 64)]
 
 
 @pytest.mark.parametrize("m,k,n", RAGGED)
