@@ -191,7 +191,11 @@ int tfb200_residual_add(const float* partial, int64_t ld_partial, const tfb200_m
  * workspace: the workspace tfb200_fused_mlp_workspace_size reports (the hidden
  * block and the RMSNorm staging) lives in a fixed TFB200_NOALLOC_SCRATCH_BYTES
  * device array that the library
- * holds on every GPU that loads it, until the process exits. Larger problems are
+ * holds on every GPU that loads it, until the process exits. With CUDA's lazy
+ * module loading (the default since CUDA 12.2) the array's memory is committed
+ * when the module loads on a device, at the latest inside the first call there;
+ * a host that reserves all of the GPU's memory makes that first call before it
+ * does (or runs with CUDA_MODULE_LOADING=EAGER). Larger problems are
  * refused with TFB200_EINVAL and a message, before any launch. The first call on
  * a device looks up the array's device address (cudaGetSymbolAddress); make that
  * first call before any stream capture. All calls on a device share the array:

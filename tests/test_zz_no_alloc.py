@@ -84,6 +84,26 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls():
     assert lib.tfb200_device_status() == L.TFB200_OK
 
 
+def test_noalloc_call_takes_no_device_memory():
+    """After the first call on the device (which may commit the scratch under lazy module loading), a call takes no
+    device memory: the device's free bytes are the same before and after it."""
+    lib = L.lib()
+    t = _case(303, 96, 256, 1024, 256)
+    x, g, w1, b1, w2 = (_dev(t[key]) for key in ("x", "gamma", "w1", "b1", "w2"))
+    y = torch.empty(x.shape[0], w2.shape[1], dtype=torch.bfloat16, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    args = [ctypes.byref(_mat(x)), ctypes.c_void_p(g.data_ptr()), ctypes.byref(_mat(w1)),
+            ctypes.c_void_p(b1.data_ptr()), ctypes.byref(_mat(w2)), ctypes.byref(_mat(x)), ctypes.c_float(1e-5),
+            ctypes.c_int(L.TFB200_GELU_TANH), ctypes.byref(_mat(y)), stream]
+    assert lib.tfb200_fused_mlp_noalloc(*args) == L.TFB200_OK, lib.tfb200_last_error()
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    assert lib.tfb200_fused_mlp_noalloc(*args) == L.TFB200_OK, lib.tfb200_last_error()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before
+    assert lib.tfb200_device_status() == L.TFB200_OK
+
+
 def test_noalloc_refuses_problems_beyond_its_scratch():
     lib = L.lib()
     m, k, h, n = 1024, 64, 8192, 64  # hidden block 16 MiB > 8 MiB
