@@ -109,8 +109,9 @@ def test_bounded_wait_reports_timeout_and_context_survives():
 def test_single_launch_mode_matches_two_launches_bit_for_bit(tmp_path):
     """The streamed MLP runs as two launches by default; TFB200_STREAM_LAUNCHES=1 runs both GEMMs in one
     cooperative launch with a grid barrier between them (measured slower, kept as an option). Both add the CTAs'
-    partial sums in the same order, so with the same grid they give the same bits. Run in child processes (the
-    switch is read once per process)."""
+    partial sums in the same order, so with the same grid they give the same bits. The L2 prefetch of the next
+    weights (TFB200_STREAM_PREFETCH=0 turns it off) changes timing only. Run in child processes (the switches are
+    read once per process)."""
     import os
     import subprocess
     import sys
@@ -131,11 +132,12 @@ def test_single_launch_mode_matches_two_launches_bit_for_bit(tmp_path):
         "y = ops.fused_mlp(x, gm, w1, b1, w2, x, 1e-5, gelu='tanh')\n"
         "np.save(sys.argv[1], y.view(torch.int16).cpu().numpy())\n")
     outs = []
-    for mode in ("2", "1"):
-        out = tmp_path / f"y{mode}.npy"
-        env = dict(os.environ, TFB200_STREAM_LAUNCHES=mode)
+    for i, extra in enumerate(({}, {"TFB200_STREAM_LAUNCHES": "1"}, {"TFB200_STREAM_PREFETCH": "0"})):
+        out = tmp_path / f"y{i}.npy"
+        env = dict(os.environ, **extra)
         r = subprocess.run([sys.executable, str(script), str(out)], env=env, capture_output=True, text=True,
                            timeout=300)
         assert r.returncode == 0, r.stderr
         outs.append(np.load(out))
     assert np.array_equal(outs[0], outs[1])
+    assert np.array_equal(outs[0], outs[2])
