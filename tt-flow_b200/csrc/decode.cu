@@ -52,7 +52,9 @@ bool two_launches() {
 // CTAs = 78 MB, inside the 126 MB L2. Measured on B200 at 32 x 8192 x 28672
 // (us per step, two runs each): none 171.9 / 172.6, 24 units 166.7 / 166.8,
 // 32 units 166.3 / 166.4, 48 units 167.5 / 167.7, 64 units 170.3 / 170.6 (the
-// prefetched tiles no longer fit beside the stream). TFB200_STREAM_PREFETCH
+// prefetched tiles no longer fit beside the stream); after the finisher
+// changes of the streaming kernel, 16 units 157.8 / 158.2, 24 units 156.1 /
+// 156.2, 32 units 155.9 / 155.9, 40 units 156.4 / 156.5. TFB200_STREAM_PREFETCH
 // overrides it (0 turns it off).
 int prefetch_units() {
   static const int n = [] {
