@@ -214,11 +214,11 @@ def test_tfb200_plan_rejects_bad_documents(doc, msg):
     assert rc == L.TFB200_EINVAL and msg in err, err
 
 
-# Measured on B200 with CUDA events (bench.py): fused MLP 8192x4096x16384 1.678 ms
-# per step, fused RMSNorm+QKV 8192x4096x6144 0.339 ms, decode MLP 32x8192x28672
-# 0.183 ms per step.
-MEASURED_S = {"b200_plan_mlp.mlir": 1.520e-3, "b200_plan_rmsnorm_matmul.mlir": 0.295e-3,
-              "b200_plan_decode.mlir": 0.177e-3}
+# Measured on B200 with CUDA events (bench.py, one CUDA graph of the timed steps): fused MLP
+# 8192x4096x16384 1.506-1.715 ms per step (box to box), fused RMSNorm+QKV 8192x4096x6144
+# 0.292-0.298 ms, decode MLP 32x8192x28672 0.154-0.158 ms.
+MEASURED_S = {"b200_plan_mlp.mlir": 1.56e-3, "b200_plan_rmsnorm_matmul.mlir": 0.295e-3,
+              "b200_plan_decode.mlir": 0.156e-3}
 
 
 @pytest.mark.parametrize("lit", sorted(MEASURED_S))
@@ -231,10 +231,10 @@ def test_time_model_tracks_measurement(lit):
     assert abs(est_s / MEASURED_S[lit] - 1.0) < 0.15, (est_s, MEASURED_S[lit])
 
 
-# Kernel time per step from the ncu launch lists summarised in profiles/ (every kernel of the step, serialised,
-# cold L2): fused MLP 8192x4096x16384 = k_gemm_pair 14177.7 us / 10 steps + k_rms_prep_reg 201.7 us / 10 steps;
-# decode MLP 32x8192x28672 = k_stream 1810.7 us / 10 steps + k_rms_prep_rows 44.7 us / 10 steps.
-NCU_S = {"b200_plan_mlp.mlir": (14177.7 + 201.7) / 10 * 1e-6, "b200_plan_decode.mlir": (1810.7 + 44.7) / 10 * 1e-6}
+# Kernel time per step from the ncu captures summarised in profiles/ (every kernel of the step, serialised,
+# cold L2): fused MLP 8192x4096x16384 = k_gemm_pair (8285.4 + 8274.3) us / 12 steps + k_rms_prep_reg 246.9 us
+# / 12 steps; decode MLP 32x8192x28672 = k_stream 91.2 + 85.7 us + k_rms_prep_rows 6.5 us.
+NCU_S = {"b200_plan_mlp.mlir": (8285.4 + 8274.3 + 246.9) / 12 * 1e-6, "b200_plan_decode.mlir": (91.2 + 85.7 + 6.5) * 1e-6}
 
 
 @pytest.mark.parametrize("lit", sorted(NCU_S))

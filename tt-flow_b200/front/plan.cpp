@@ -30,12 +30,12 @@ constexpr int64_t kStreamBudget = cfg::kStreamBudget, kStreamAcc = cfg::kStreamA
 constexpr double kLaunchSeconds = 3e-6;  // per kernel launch boundary (ramp up / drain)
 // Fractions of the measured peaks the kernels sustain, measured on B200 with
 // CUDA events: the tcgen05 GEMM ran the fused MLP 8192x4096x16384 at
-// 1428-1466 TFLOP/s (87-90 % of 1635.3) and the fused RMSNorm+MatMul
-// 8192x4096x6144 at 1398 TFLOP/s (85.5 %); the weight-streaming kernels ran the
-// decode MLP 32x8192x28672 at 5262-5331 GB/s (80.5-81.6 % of 6534.5).
+// 1356-1460 TFLOP/s (82-88 % of 1662.2) and the fused RMSNorm+MatMul
+// 8192x4096x6144 at 1384-1411 TFLOP/s (83-85 %); the weight-streaming kernels
+// ran the decode MLP 32x8192x28672 at 5961-6108 GB/s (91-93.5 % of 6534.5).
 // (spec/devices.json "model" records both with their basis.)
 constexpr double kTensorEfficiency = 0.87;
-constexpr double kHbmEfficiency = 0.81;
+constexpr double kHbmEfficiency = 0.93;
 
 std::string q(const std::string& s) { return "\"" + s + "\""; }
 
