@@ -2,12 +2,14 @@
 // weights. HBM-bound: the job is to stream the weights at full bandwidth from
 // every SM.
 //
-// One persistent launch runs the MLP's two GEMMs as two phases,
+// One persistent launch runs one GEMM, or the MLP's two GEMMs as two phases,
 //   phase 0: h   = epi0(A0[M, K0] @ W0[K0, N0])   (up-projection, h in HBM/L2)
 //   phase 1: out = epi1(h[M, N0]  @ W1[N0, N1])   (down-projection)
 // with a grid-wide barrier between them (a counter the RMSNorm staging pass
 // zeroes; one CTA per SM, launched cooperatively so that every CTA is resident
-// together whatever else runs on the GPU). Each GEMM is computed as the
+// together whatever else runs on the GPU). The decode MLP (decode.cu) runs the
+// two GEMMs as two one-phase launches by default, which measured faster; the
+// two-phase launch gives the same bits. Each GEMM is computed as the
 // transposed product acc^T = W^T A^T ("swap AB"): the MMA's M side is 128
 // output features (W columns, read N-major straight from row-major W) and its
 // N side is the token count rounded up to 32. Work units are (128-column block,
