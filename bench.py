@@ -293,7 +293,8 @@ def run_reference(args) -> int:
                    "sample_rows_per_step": info["rows"]},
         "cpu_baseline": {"value": value, "unit": unit, "cores": info["cores"], "kind": "port",
                          "sample": f"{info['rows']} of {d['M']} rows per step, numpy/OpenBLAS fp32 matmuls, "
-                                   f"libm erf per element"},
+                                   f"libm erf per element; the sampled rows' rate extrapolated to the workload "
+                                   f"(a row sample runs OpenBLAS below its full-M rate)"},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -596,7 +597,8 @@ def run_ours(args) -> int:
             v = v * 1e12 / flops_step * W.algorithmic_bytes(name) / 1e9
         line["cpu_baseline"] = {"value": v, "unit": unit, "cores": info["cores"], "kind": "port",
                                 "sample": f"{info['rows']} of {d['M']} rows in {sec:.1f} s: the reference golden "
-                                          f"restated (numpy/OpenBLAS fp32, libm erf per element)"}
+                                          f"restated (numpy/OpenBLAS fp32, libm erf per element); the sampled "
+                                          f"rows' rate extrapolated to the workload"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     del graph
