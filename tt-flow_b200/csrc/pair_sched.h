@@ -1,7 +1,8 @@
 // Work schedule of the persistent CTA-pair GEMM (k_gemm_pair): which output
 // tiles and which k-block ranges each CTA pair processes. Shared by the kernel
-// (device), the launcher (host) and the planner (front/plan.cpp), so that all
-// three agree on the split; plain C++ apart from the qualifiers.
+// (device) and the launcher (host), so that both agree on the split, and
+// checked exhaustively on the CPU by tests/native/sched_check.cpp; plain C++
+// apart from the qualifiers.
 //
 // With T output tiles of KB k-blocks on P resident pairs, T / P full waves run
 // data parallel (pair p takes tiles p, p + P, ...). When T is not a multiple of
