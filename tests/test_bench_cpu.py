@@ -41,3 +41,18 @@ def test_reference_arm_other_ranks_exit_quietly():
     r = _run({"RANK": "1", "WORLD_SIZE": "2"}, "--workload", "mlp_block_small", "--steps", "1", "--warmup", "0")
     assert r.returncode == 0, r.stderr
     assert not [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+
+
+def test_traffic_table_names_real_workloads():
+    """The per-launch DRAM traffic the GPU arm reports (from the ncu captures in profiles/) is keyed by workload
+    name: every key must be a workload, and each figure must lie between a quarter of the step's algorithmic bytes
+    and ten times them (a misplaced decimal or a figure for the wrong workload would fall outside)."""
+    sys.path[:0] = [str(ROOT), str(ROOT / "tt-flow_b200")]
+    import bench
+    from tfb200 import workloads as W
+
+    assert bench.TRAFFIC_BYTES_PER_LAUNCH
+    for name, traffic in bench.TRAFFIC_BYTES_PER_LAUNCH.items():
+        assert name in W.WORKLOADS, name
+        step_bytes = W.algorithmic_bytes(name)
+        assert step_bytes / 4 < traffic < 10 * step_bytes, (name, traffic, step_bytes)
